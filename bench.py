@@ -1,0 +1,337 @@
+"""Benchmark of the bfp16 weight-GEMM hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
+
+Workload (the DiT FFN up-projection; one per GPU, data-parallel): X[4352, 3072] ~ N(0,1) bf16,
+W[3072, 12288] ~ N(0, 0.02) packed to bfp16, bias ~ N(0, 0.01); one step = quantise X to bfp16 (bit-exact with the
+reference) + the packed-weight GEMM with the bias epilogue, fp32 accumulation, bf16 out. The metric is the
+reference's headline "bfp16 GEMM TFLOP/s" (2*M*N*K per step, quantiser time included). Inputs rotate over three
+independent sets (3 x 69 MB of X + packed W > the 126 MB L2), so every step reads its operands from HBM.
+
+--impl reference times the reference's own CPU path (its numpy bfp16 quantisation + decode + float32 matmul,
+restated in oracle/bfp16_oracle.py) on the host cores, on a bounded row sample per step.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K, N = 4352, 3072, 12288
+FLOP = 2.0 * M * N * K
+WORKLOAD = "C1: bfp16 linear X[4352,3072] @ W[3072,12288] + bias, bf16 out (DiT FFN up-projection)"
+METRIC = "bfp16 GEMM TFLOP/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-rows", type=int, default=128, help="reference arm: X rows per step (bounded sample)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def ncu_traffic():
+    """dram read+write bytes per launch of the GEMM, from the committed ncu summary (None if absent)."""
+    p = os.path.join(ROOT, "profiles", "bfp16_linear_c1.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every ~5 ms while the timed region runs."""
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        names = {getattr(nv, k): k for k in dir(nv) if k.startswith("nvmlClocksEventReason") or
+                 k.startswith("nvmlClocksThrottleReason")}
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h) if hasattr(
+                    nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for bit, name in ((0x8, "hw_slowdown"), (0x40, "hw_thermal_slowdown"), (0x20, "sw_thermal_slowdown"),
+                                  (0x4, "sw_power_cap"), (0x80, "hw_power_brake_slowdown")):
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nv:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        s = sorted(self.samples)
+        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(s)}
+
+
+def dist_init(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=120))
+    return ws, rank, local
+
+
+def cpu_baseline_sample(rows):
+    """The reference's CPU path on `rows` rows of config 1 (oracle restatement, numpy + OpenBLAS on all cores):
+    quantise X to bfp16 in the A layout, decode, float32 matmul against the decoded packed W (decoded once, like
+    the resident weights). Returns (TFLOP/s, seconds, threads)."""
+    import numpy as np
+    from oracle import bfp16_oracle as O
+    rng = np.random.default_rng(0)
+    x = O.bf16_round(rng.standard_normal((rows, K)).astype(np.float32))
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    wd = O.unpack_b(O.pack_b(W), K, N)
+    bias = O.bf16_round((rng.standard_normal(N) * 0.01).astype(np.float32))
+    t = time.perf_counter()
+    q = O.to_bfp16(O.a_layout(x, 128, 64)) if rows % 128 == 0 else O.to_bfp16(x)
+    xd = O.from_bfp16(q).astype(np.float32)
+    xd = O.a_unlayout(xd, rows, K) if rows % 128 == 0 else xd.reshape(rows, K)
+    c = O.linear(xd, wd, bias)
+    dt = time.perf_counter() - t
+    del c
+    return 2.0 * rows * N * K / dt / 1e12, dt, len(os.sched_getaffinity(0))
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import bfp16_oracle as O
+    rows = args.ref_rows
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    wd = O.unpack_b(O.pack_b(W), K, N)
+    bias = O.bf16_round((rng.standard_normal(N) * 0.01).astype(np.float32))
+    xs = [O.bf16_round(rng.standard_normal((rows, K)).astype(np.float32)) for _ in range(3)]
+
+    def step(i):
+        x = xs[i % 3]
+        q = O.to_bfp16(O.a_layout(x, 128, 64)) if rows % 128 == 0 else O.to_bfp16(x)
+        xd = O.from_bfp16(q).astype(np.float32)
+        xd = O.a_unlayout(xd, rows, K) if rows % 128 == 0 else xd.reshape(rows, K)
+        return O.linear(xd, wd, bias)
+
+    for i in range(args.warmup):
+        step(i)
+    t = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t
+    value = 2.0 * rows * N * K * args.steps / dt / 1e12
+    cores = len(os.sched_getaffinity(0))
+    out = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": ws,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "parallelism": "host cores",
+                      "sample_rows_per_step": rows},
+           "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                            "sample": f"{rows} of {M} rows of X per step (to_bfp16(a_layout) + from_bfp16 + "
+                                      f"float32 matmul vs the decoded packed W, numpy/OpenBLAS, "
+                                      f"OPENBLAS_NUM_THREADS={os.environ.get('OPENBLAS_NUM_THREADS', 'all')})"},
+           "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    import numpy as np
+    import torch
+    from redline_tiny_b200 import ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    sets = []
+    for s in range(3):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        W = torch.randn((K, N), generator=g, device=dev) * 0.02
+        w = ops.PackedWeight.from_float(W)
+        del W
+        b = (torch.randn((N,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        sets.append((x, w, b))
+    dq = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream()
+
+    # the timed loop calls the C ABI directly on preallocated buffers (no allocation inside a step)
+    from redline_tiny_b200 import _lib as L
+
+    def quant(x):
+        L.call("rl_quantize_bfp16", x.data_ptr(), L.RL_BF16, M, K, L.RL_ROWMAJOR, None, dq.data_ptr(),
+               stream.cuda_stream)
+
+    def step(i, ev=None):  # quantiser + GEMM
+        x, w, b = sets[i % 3]
+        quant(x)
+        if ev is not None:
+            ev[0].record(stream)
+        L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, b.data_ptr(), L.RL_EPI_BIAS,
+               out.data_ptr(), L.RL_BF16, stream.cuda_stream)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ops.device_status()
+
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    gemm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i, gemm_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    gemm_ms = sum(a.elapsed_time(b) for a, b in gemm_ev) / args.steps
+    if ws > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.barrier()
+    ops.device_status()
+
+    # end to end through the public API with host buffers: pinned X in, quantise + GEMM, C back to pinned memory
+    xh = [sets[s][0].cpu().pin_memory() for s in range(3)]
+    xd = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    oh = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step(i):
+        xd.copy_(xh[i % 3], non_blocking=True)
+        quant(xd)
+        x, w, b = sets[i % 3]
+        L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, b.data_ptr(), L.RL_EPI_BIAS,
+               out.data_ptr(), L.RL_BF16, stream.cuda_stream)
+        oh.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    if rank != 0:
+        if ws > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    pk, pk_kind = peaks()
+    peak = pk["bf16_tflops"]
+    achieved = FLOP / (gemm_ms * 1e-3) / 1e12
+    traffic = ncu_traffic()
+    value = FLOP * args.steps * ws / (ms * 1e-3) / 1e12
+    res = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "global_batch": ws,
+                      "parallelism": f"dp{ws} (one config-1 GEMM per GPU, no collective)",
+                      "l2": "inputs rotate over 3 sets (X + packed W + out = 176 MB per step > 126 MB L2)"},
+           "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak, "traffic": traffic,
+                        "kernel": "bfp16_linear_kernel", "peak_kind": f"{pk_kind} bf16 dense (burst)",
+                        "algorithmic_flop_per_launch": FLOP},
+           "clocks": clk.summary(),
+           "e2e": {"value": FLOP * e2e_steps * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                   "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+           "gpu_launches": 2 * args.steps,
+           "kernel_ms": {"bfp16_linear": gemm_ms, "quantize+linear": ms / args.steps}}
+    if ws == 1 and not args.no_cpu_baseline:
+        tf, dt, cores = cpu_baseline_sample(M)
+        res["cpu_baseline"] = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                               "sample": f"config 1 in full ({M} rows) once: to_bfp16(a_layout) + from_bfp16 + "
+                                         f"float32 matmul with bias, numpy/OpenBLAS, {dt:.2f} s"}
+    print(json.dumps(res), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_init(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,125 @@
+/*
+ * redline_b200.h - C ABI of the B200 (sm_100a) bfp16 weight-GEMM hot path.
+ *
+ * Drop-in boundary for Cukrus-directive/redline-tiny's matrix-multiply path. The reference crosses its device boundary
+ * in Python, at `NPU.run(op, artifact, [iron tensors])` (redline/forward.py:138-165) and `gemm()`
+ * (redline/forward.py:194-197); its data formats are defined by redline/npu_layouts.py and
+ * redline/pack_weights.py. Each entry point below names the reference interface it replaces.
+ *
+ * Conventions (all entry points):
+ *  - Plain device pointers and sizes; the caller owns every buffer (the reference's kernels also write caller-
+ *    allocated iron tensors in place). Nothing here allocates device memory.
+ *  - Calls are stream-ordered and asynchronous on `stream` (0 = the legacy default stream). Buffers must stay alive
+ *    until the stream reaches the call (forward.py:151-153 states the same rule for the NPU).
+ *  - Return 0 (RL_OK) or a negative rl_status; rl_last_error() gives the message (thread-local). Kernels never trap:
+ *    a device-side failure (a bounded wait that ran out, a skipped out-of-range access) sets a device error word that
+ *    rl_device_status() reads and clears.
+ *  - bfp16 ("bfp16ebs8"): blocks of 8 consecutive values, 9 bytes each = [E][m0..m7], value = m * 2^(E - 133).
+ *  - bf16 buffers are passed as uint16_t bit patterns.
+ */
+#ifndef REDLINE_B200_H
+#define REDLINE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* rl_stream_t; /* the same handle as cudaStream_t / CUstream */
+
+typedef enum {
+  RL_OK = 0,
+  RL_ERR_ARGUMENT = -1,    /* bad shape, null pointer or unknown enum */
+  RL_ERR_ALIGNMENT = -2,   /* a pointer or a size breaks the documented alignment */
+  RL_ERR_UNSUPPORTED = -3, /* valid request this build does not implement (e.g. no sm_100 device) */
+  RL_ERR_CUDA = -4,        /* a CUDA runtime / driver call failed */
+  RL_ERR_DEVICE = -5       /* rl_device_status: a kernel reported a device-side error */
+} rl_status;
+
+typedef enum { RL_F32 = 0, RL_BF16 = 1 } rl_dtype;
+
+/* Stream order of bfp16 blocks. RL_ROWMAJOR: block (r, c/8) of an (M, K) matrix at index r*K/8 + c/8.
+ * RL_A_LAYOUT: the reference's GEMM A-operand order, a_layout(A, 128, 64) (npu_layouts.py:18-23). */
+typedef enum { RL_ROWMAJOR = 0, RL_A_LAYOUT = 1 } rl_layout;
+
+typedef enum {
+  RL_EPI_NONE = 0,   /* C = A @ B */
+  RL_EPI_BIAS = 1,   /* C = A @ B + bias[N] */
+  RL_EPI_SWIGLU = 2  /* weights packed with swiglu_interleaved=1; C[M, N/2] = silu(gate) * proj (+ bias first) */
+} rl_epilogue;
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* rl_last_error(void);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int rl_version(void);
+
+/* Synchronise the current device, then read and clear the device error word (bit 1: a bounded wait ran out;
+ * bit 2: a kernel-side range check skipped an access). Returns RL_ERR_DEVICE when any bit was set. */
+int rl_device_status(int* flags_out);
+
+/*
+ * a1/a3 - activation quantiser. Replaces npu_layouts.to_bfp16 (redline/npu_layouts.py:62-88) applied to
+ * a_layout(x, 128, 64) (npu_layouts.py:18-23), as forward.py:406 and forward.py:613 call it.
+ * x: (M, K) row-major, dtype RL_F32 or RL_BF16, K % 8 == 0, 16-byte aligned.
+ * q_out (may be NULL): M*K/8*9 bytes of bfp16, bit-identical to the reference, in `layout` order
+ *   (RL_A_LAYOUT needs M % 128 == 0 and K % 64 == 0).
+ * dq_out (may be NULL): the decoded values as bf16 (M, K) row-major - the A operand rl_linear_bfp16 takes.
+ */
+int rl_quantize_bfp16(const void* x, int x_dtype, int64_t M, int64_t K, int layout, uint8_t* q_out,
+                      uint16_t* dq_out, rl_stream_t stream);
+
+/*
+ * a2 - decoder. Replaces npu_layouts.from_bfp16 (redline/npu_layouts.py:90-94) followed by a_unlayout
+ * (npu_layouts.py:56-60) when layout == RL_A_LAYOUT. out: (M, K) row-major, RL_F32 or RL_BF16 (both exact).
+ */
+int rl_dequantize_bfp16(const uint8_t* q, int layout, int64_t M, int64_t K, void* out, int out_dtype,
+                        rl_stream_t stream);
+
+/*
+ * a4/a6 - the reference's packed-weight stream on the GPU. Replaces pack_weights.pack_b
+ * (redline/pack_weights.py:72-79): out = to_bfp16(b_layout(B, 64, 128)), bit-identical.
+ * B: (K, N) row-major (B = W^T, C = A @ B), RL_F32 or RL_BF16; K % 64 == 0, N % 128 == 0.
+ */
+int rl_pack_b(const void* B, int dtype, int64_t K, int64_t N, uint8_t* out, rl_stream_t stream);
+
+/*
+ * a6 - load-time repack of the reference's packed stream (the bytes of bNN_*.bin, pack_weights.py:106-112) into the
+ * GPU-native tile format the GEMM streams. Lossless (the same blocks, reordered), 1.125 B per weight.
+ * Native tile (128 columns x 64 K, 9216 B; N-tile outer, K-tile inner, like b_layout):
+ *   bytes [0, 8192): mantissas in offset binary (m + 128), 16-byte chunk (j, n) at (j * 128 + n) * 16 = blocks 2j
+ *                    and 2j+1 of column n;
+ *   bytes [8192, 9216): exponents, column n at 8192 + n * 8, one byte per 8-row block.
+ * swiglu_interleaved = 1: B is an up matrix with [gate 64 | proj 64] per 128-column tile (pack_weights.py:82-89);
+ *   the native rows are permuted so each 32-row quarter holds 16 gate units then the same 16 proj units.
+ */
+int rl_weights_from_pack_b(const uint8_t* packed, int64_t K, int64_t N, int swiglu_interleaved, uint8_t* native,
+                           rl_stream_t stream);
+
+/* Pack float B (K, N) directly into the native format (equals rl_weights_from_pack_b(rl_pack_b(B))). */
+int rl_pack_weights(const void* B, int dtype, int64_t K, int64_t N, int swiglu_interleaved, uint8_t* native,
+                    rl_stream_t stream);
+
+/*
+ * a7/a8/a9 - the packed-weight GEMM. Replaces gemm(npu, w, op, M, a, c) (redline/forward.py:194-197), which runs
+ * matmul_vectorized_bfp16 (kernels/atb3/mm_bfp_rho.cc:64-177) and, for the up projection,
+ * matmul_swiglu_bfp16 (kernels/atb3/mm_bfp_swiglu.cc:88-168).
+ * x: (M, K) bf16 row-major holding bfp16-exact values (rl_quantize_bfp16's dq_out), 16-byte aligned, K % 64 == 0.
+ * w_native: rl_weights_from_pack_b / rl_pack_weights output for B (K, N), N % 128 == 0.
+ * bias: bf16 [N] or NULL (required for RL_EPI_BIAS).
+ * out: (M, N) row-major (RL_EPI_SWIGLU: (M, N/2)), RL_BF16 or RL_F32. fp32 accumulation on tcgen05 tensor cores.
+ */
+int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                    const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream);
+
+/* GEMM kernel variant for tests and benchmarks: 0 = default (= 2), 1 = weights decoded into shared memory (MMA A
+ * operand from shared memory), 2 = weights decoded into tensor memory (A from TMEM); tuning codes
+ * 1000*P + 100*G + 10*V + S also select the decode split and the pipeline depth. Returns the previous value. */
+int rl_set_gemm_variant(int variant);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REDLINE_B200_H */

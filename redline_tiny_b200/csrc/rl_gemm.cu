@@ -1,0 +1,468 @@
+// Packed-weight bfp16 GEMM on tcgen05 tensor cores (sm_100a).
+//
+// Computes C[M, N] = X[M, K] @ B[K, N] where X is bf16 holding bfp16-exact values and B is streamed in the native
+// packed tile format (1.125 B per weight; see rl_weights_from_pack_b). The weights sit on the MMA's M side:
+//   D^T tile [128 weight columns (TMEM lanes)] x [256 activation rows (TMEM columns)], fp32 in tensor memory,
+//   D^T += W^T[128 x K] * X[256 x K]^T, issued as tcgen05.mma kind::f16 M=128 N=256 K=16.
+// Per 64-deep K step a pipeline stage holds
+//   X tile   256 x 64 bf16, loaded by TMA with the 128-byte swizzle (the MMA's B operand, K-major);
+//   W9 tile  128 x 64 bfp16 in native order, 9216 contiguous bytes, loaded by one bulk copy;
+// and expander warps decode the W9 tile to bf16 (exact: int8 * 2^e fits bf16) into the MMA's A operand:
+//   variant kSmemA: a 128 x 64 bf16 tile in shared memory, in the 128-byte-swizzled K-major layout;
+//   variant kTmemA: tensor memory, one lane per weight column, 2 bf16 per 32-bit column (tcgen05.st), which keeps
+//                   the decoded operand out of shared memory entirely (no write, no MMA re-read).
+// Decoding is the throughput limiter (16 weights per MMA cycle per SM), so it is spread over 4*P*G warps: P parts
+// split one stage's eight 8-deep blocks, G groups take alternate stages.
+// Warp roles: warp 0 = TMA producer + TMEM allocator, warp 1 = MMA issuer, then the expanders, then 8 epilogue
+// warps (tcgen05.ld of D, bias / SwiGLU, transposed through shared memory into row-major C). The accumulator is
+// single-buffered in TMEM (the decoded A stages take the rest), so two warps per lane quarter drain it in halves
+// and release it as soon as their last tcgen05.ld has landed, before the last stores.
+// The kernel is persistent: one CTA per SM walks tiles (activation-tile fastest, so the CTAs in flight share the
+// same weight columns and the whole X in L2).
+#include <cmath>
+
+#include "rl_common.cuh"
+#include "rl_host.h"
+
+namespace rl {
+namespace gemm {
+
+constexpr int BM = 128;                 // weight columns per tile = MMA M = TMEM lanes
+constexpr int BN = 256;                 // activation rows per tile = MMA N
+constexpr int BK = 64;                  // K per pipeline stage
+constexpr int UK = 16;                  // K per tcgen05.mma (kind::f16)
+constexpr int X_BYTES = BN * BK * 2;    // 32768
+constexpr int WE_BYTES = BM * BK * 2;   // 16384 (decoded weights, shared-memory variant)
+constexpr int W9_BYTES = 9216;          // one native weight tile
+constexpr int kChunk = 16;              // epilogue: D columns (activation rows) per tcgen05.ld
+constexpr int kEpiStageBytes = kChunk * 32 * 4;  // per epilogue warp: 16 rows x 32 columns x fp32
+
+enum Variant { kSmemA = 1, kTmemA = 2 };
+
+template <int V, int S, int G, int P>
+struct Cfg {
+  static constexpr int kStages = S;
+  static constexpr int kGroups = G;
+  static constexpr int kParts = P;
+  static constexpr int kExpWarps = 4 * P * G;
+  static constexpr int kEpiWarps = 8;                                          // 2 per TMEM lane quarter
+  static constexpr int kWarps = 2 + kExpWarps + kEpiWarps;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kEpiWarp0 = 2 + kExpWarps;
+  static constexpr int kXOff = 0;                                              // S x 32 KB, 1024-aligned
+  static constexpr int kWEOff = kXOff + S * X_BYTES;                           // SS: S x 16 KB, 1024-aligned
+  static constexpr int kW9Off = kWEOff + (V == kSmemA ? S * WE_BYTES : 0);     // S x 9216 B, 16-aligned
+  static constexpr int kEpiOff = kW9Off + S * W9_BYTES;
+  static constexpr int kBarOff = kEpiOff + kEpiWarps * kEpiStageBytes;
+  static constexpr int kAccBufs = (V == kSmemA) ? 2 : 1;                       // TMEM D buffers of 256 columns
+  static constexpr int kTmemACol = 256;                                        // TS: A stages after one D buffer
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOff + 256;
+  static_assert(V == kSmemA || 256 + S * (BK / 2) <= 512, "TMEM: one D buffer + S A stages");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(S <= 8 && G >= 1 && G <= 4 && (P == 1 || P == 2), "config");
+};
+
+struct Params {
+  const uint8_t* w9;     // native weight tiles
+  const uint16_t* bias;  // bf16 [N] or null
+  void* out;
+  int64_t M, N, K;
+  int out_f32;           // 1: fp32 output, 0: bf16
+  int epilogue;          // RL_EPI_*
+  int num_x_tiles, num_w_tiles, num_tiles, KT;
+};
+
+struct Barriers {
+  uint64_t full[8];      // producer tx: X + W9 landed
+  uint64_t expf[8];      // expanders: decoded A stage ready
+  uint64_t empty[8];     // MMA commit: stage consumed
+  uint64_t accf[2];      // MMA commit: accumulator complete
+  uint64_t acce[2];      // epilogue: accumulator drained
+  uint64_t drain;        // error path: wait for MMAs in flight
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+// Epilogue of one 16-column chunk of D (16 activation rows x this warp's 32 weight columns): bias, SwiGLU or plain
+// conversion, transposed through the warp's staging buffer into row-major global memory.
+__device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&r)[kChunk], uint8_t* st, int lane,
+                                               int q, int wt, int64_t x0, float bias_v) {
+  if (p.epilogue == RL_EPI_SWIGLU) {
+    // lanes 0-15: gate of units 16q + lane; lanes 16-31: proj of the same units
+    uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const float v = __uint_as_float(r[j]) + bias_v;
+      const float pv = __shfl_down_sync(0xffffffffu, v, 16);
+      const float h = silu_f(v) * pv;
+      // round h to bfp16 with blocks of 8 consecutive units (8 lanes), as the down GEMM's A operand
+      const uint32_t hb = __float_as_uint(h);
+      uint32_t e = (hb >> 23) & 0xFFu;
+      e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
+      e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
+      e = max(e, __shfl_xor_sync(0xffffffffu, e, 4));
+      const int m = bfp16_quant_one(hb, e);
+      const float dq = __fmul_rn(static_cast<float>(m), bfp16_scale(e));
+      if (lane < 16) s16[j * 16 + lane] = static_cast<uint16_t>(__float_as_uint(dq) >> 16);
+    }
+    __syncwarp();
+    // 16 rows x 16 units bf16 = 32 B per row: 32 pieces of 16 bytes, one per lane
+    const int64_t Nout = p.N / 2;
+    uint16_t* outp = static_cast<uint16_t*>(p.out);
+    const int rr = lane >> 1, part = lane & 1;
+    const int64_t xr = x0 + rr;
+    if (xr < p.M)
+      *reinterpret_cast<uint4*>(outp + xr * Nout + static_cast<int64_t>(wt) * 64 + 16 * q + part * 8) =
+          reinterpret_cast<const uint4*>(s16 + rr * 16)[part];
+    __syncwarp();
+  } else if (!p.out_f32) {
+    uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j)
+      s16[j * 32 + lane] = static_cast<uint16_t>(float_to_bf16_bits(__uint_as_float(r[j]) + bias_v));
+    __syncwarp();
+    uint16_t* outp = static_cast<uint16_t*>(p.out);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = lane + 32 * i, rr = idx >> 2, part = idx & 3;
+      const int64_t xr = x0 + rr;
+      if (xr < p.M)
+        *reinterpret_cast<uint4*>(outp + xr * p.N + static_cast<int64_t>(wt) * BM + 32 * q + part * 8) =
+            reinterpret_cast<const uint4*>(s16 + rr * 32)[part];
+    }
+    __syncwarp();
+  } else {
+    float* s32 = reinterpret_cast<float*>(st);
+    float* outp = static_cast<float*>(p.out);
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) s32[j * 32 + lane] = __uint_as_float(r[j]) + bias_v;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = lane + 32 * i, rr = idx >> 3, part = idx & 7;
+      const int64_t xr = x0 + rr;
+      if (xr < p.M)
+        *reinterpret_cast<uint4*>(outp + xr * p.N + static_cast<int64_t>(wt) * BM + 32 * q + part * 4) =
+            reinterpret_cast<const uint4*>(s32 + rr * 32)[part];
+    }
+    __syncwarp();
+  }
+}
+
+template <int V, int S, int G, int P>
+__global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
+    bfp16_linear_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  using C = Cfg<V, S, G, P>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi_stage = smem + C::kEpiOff;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + C::kBarOff);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  auto stage_x = [&](int s) { return smem + C::kXOff + s * X_BYTES; };
+  auto stage_we = [&](int s) { return smem + C::kWEOff + s * WE_BYTES; };
+  auto stage_w9 = [&](int s) { return smem + C::kW9Off + s * W9_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->expf[s], 4 * P);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->accf[b], 1);
+      mbar_init(&bars->acce[b], C::kEpiWarps);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const int KT = p.KT;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int kiter = 0;
+      uint32_t issued = 0, last_par = 0;  // per-stage bit masks (error-path drain)
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int xt = tile % p.num_x_tiles, wt = tile / p.num_x_tiles;
+        const uint8_t* wsrc = p.w9 + static_cast<int64_t>(wt) * KT * W9_BYTES;
+        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+          const int s = kiter % C::kStages;
+          const uint32_t ph = (kiter / C::kStages) & 1;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->full[s], X_BYTES + W9_BYTES);
+          tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN);
+          bulk_load(stage_w9(s), wsrc + static_cast<int64_t>(kt) * W9_BYTES, W9_BYTES, &bars->full[s]);
+          issued |= 1u << s;
+          last_par = (last_par & ~(1u << s)) | (ph << s);
+        }
+      }
+      if (!ok) {  // let copies already in flight land before the CTA can exit
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued & (1u << s)) mbar_drain(&bars->full[s], (last_par >> s) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      int kiter = 0, it = 0;
+      bool ok = true, any = false;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+        const int b = (C::kAccBufs == 2) ? (it & 1) : 0;
+        const int use = (C::kAccBufs == 2) ? (it >> 1) : it;
+        if (!mbar_wait(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + b * 256;
+        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+          const int s = kiter % C::kStages;
+          const uint32_t ph = (kiter / C::kStages) & 1;
+          if (!mbar_wait(&bars->full[s], ph, abort) || !mbar_wait(&bars->expf[s], ph, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(stage_x(s)));
+          if constexpr (V == kSmemA) {
+            const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(stage_we(s)));
+#pragma unroll
+            for (int k = 0; k < BK / UK; ++k)
+              umma_ss(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+          } else {
+            const uint32_t a_tmem = tmem + C::kTmemACol + s * (BK / 2);
+#pragma unroll
+            for (int k = 0; k < BK / UK; ++k)
+              umma_ts(d_tmem, a_tmem + k * (UK / 2), bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+          }
+          any = true;
+          umma_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bars->accf[b]);
+      }
+      if (!ok && any) {  // no MMA may still be reading TMEM / shared memory when the CTA exits
+        umma_commit(&bars->drain);
+        mbar_drain(&bars->drain, 0);
+      }
+    }
+  } else if (warp < C::kEpiWarp0) {
+    // ---------------- expanders: W9 (bfp16) -> bf16 A operand ----------------
+    constexpr int BPP = 8 / P;                 // 8-deep blocks per part
+    const int e = warp - 2;
+    const int q = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = 32 * q + lane;             // weight column within the tile
+    const int part = (e >> 2) % P;             // which blocks of the stage
+    const int grp = (e >> 2) / P;              // which stages: kiter % G == grp
+    int kiter = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int kt = 0; kt < KT; ++kt, ++kiter) {
+        if (G > 1 && (kiter % G) != grp) continue;
+        const int s = kiter % C::kStages;
+        const uint32_t ph = (kiter / C::kStages) & 1;
+        if (!mbar_wait(&bars->full[s], ph, abort)) { ok = false; break; }
+        const uint8_t* w9 = stage_w9(s);
+        const uint2 ex = *reinterpret_cast<const uint2*>(w9 + 8192 + row * 8);
+        uint4 mq[BPP / 2];
+#pragma unroll
+        for (int j = 0; j < BPP / 2; ++j)
+          mq[j] = *reinterpret_cast<const uint4*>(w9 + ((part * (BPP / 2) + j) * 128 + row) * 16);
+        uint32_t words[4 * BPP];
+#pragma unroll
+        for (int b = 0; b < BPP; ++b) {
+          const int bk = part * BPP + b;
+          const uint32_t E = __byte_perm(bk < 4 ? ex.x : ex.y, 0u, 0x4440u + (bk & 3));
+          const uint32_t u0 = (b & 1) ? mq[b >> 1].z : mq[b >> 1].x;
+          const uint32_t u1 = (b & 1) ? mq[b >> 1].w : mq[b >> 1].y;
+          uint32_t w[4];
+          bfp16_decode_block_ob(E, u0, u1, w);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) words[b * 4 + i] = w[i];
+        }
+        if constexpr (V == kSmemA) {
+          uint8_t* we = stage_we(s) + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int b = 0; b < BPP; ++b) {
+            const int bk = part * BPP + b;
+            *reinterpret_cast<uint4*>(we + ((bk ^ (row & 7)) << 4)) =
+                make_uint4(words[b * 4], words[b * 4 + 1], words[b * 4 + 2], words[b * 4 + 3]);
+          }
+          fence_proxy_async_smem();
+        } else {
+          tc_fence_after();
+          const uint32_t taddr = tmem + C::kTmemACol + s * (BK / 2) + part * (BK / 2 / P) + ((32u * q) << 16);
+          if constexpr (P == 1) {
+            RL_TMEM_ST32(taddr, words);
+          } else {
+            RL_TMEM_ST16(taddr, words);
+          }
+          tmem_st_wait_regs(words);
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->expf[s]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: 8 warps, (lane quarter q, column half h) each ----------------
+    const int ew = warp - C::kEpiWarp0;
+    const int q = warp & 3;
+    const int h = ew >> 2;                         // activation-row half of the tile: columns [128h, 128h + 128)
+    const int row = 32 * q + lane;                 // weight column within the tile (native order)
+    uint8_t* st = epi_stage + ew * kEpiStageBytes;
+    constexpr int NC = BN / 2 / kChunk;            // 8 chunks of 16 columns per warp
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const int xt = tile % p.num_x_tiles, wt = tile / p.num_x_tiles;
+      const int b = (C::kAccBufs == 2) ? (it & 1) : 0;
+      const int use = (C::kAccBufs == 2) ? (it >> 1) : it;
+      float bias_v = 0.0f;
+      if (p.bias) {
+        // native row -> output column (SwiGLU permutes rows inside the tile)
+        int col = row;
+        if (p.epilogue == RL_EPI_SWIGLU) col = (lane < 16 ? 0 : 64) + 16 * q + (lane & 15);
+        bias_v = bf16_bits_to_float(p.bias[static_cast<int64_t>(wt) * BM + col]);
+      }
+      if (!mbar_wait(&bars->accf[b], use & 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tbase = tmem + b * 256 + h * (BN / 2) + ((32u * q) << 16);
+      const int64_t xb = static_cast<int64_t>(xt) * BN + h * (BN / 2);
+      // chunk by chunk: the tcgen05.ld of chunk c+1 is in flight while chunk c is converted and stored
+      uint32_t ra[kChunk], rb[kChunk];
+      RL_TMEM_LD16(tbase, ra);
+      tmem_ld_wait_regs(ra);
+#pragma unroll 1
+      for (int c = 0; c < NC; c += 2) {
+        RL_TMEM_LD16(tbase + (c + 1) * kChunk, rb);
+        epilogue_chunk(p, ra, st, lane, q, wt, xb + c * kChunk, bias_v);
+        tmem_ld_wait_regs(rb);
+        if (c + 2 < NC) {
+          RL_TMEM_LD16(tbase + (c + 2) * kChunk, ra);
+        } else {  // every column of D is in registers: hand the accumulator back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->acce[b]);
+        }
+        epilogue_chunk(p, rb, st, lane, q, wt, xb + (c + 1) * kChunk, bias_v);
+        if (c + 2 < NC) tmem_ld_wait_regs(ra);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+static int g_variant = 0;  // 0 = default
+
+template <int V, int S, int G, int P>
+int launch(const CUtensorMap& tmap, const Params& p, cudaStream_t stream) {
+  using C = Cfg<V, S, G, P>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    RL_TRY_CUDA(cudaFuncSetAttribute(bfp16_linear_kernel<V, S, G, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+  bfp16_linear_kernel<V, S, G, P><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tmap, p);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S); 0 = default.
+int dispatch(int code, const CUtensorMap& tmap, const Params& p, cudaStream_t stream) {
+  switch (code) {
+    case 1:
+    case 1213: return launch<kSmemA, 3, 2, 1>(tmap, p, stream);
+    case 1125: return launch<kTmemA, 5, 1, 1>(tmap, p, stream);
+    case 0:
+    case 2:
+    case 1225: return launch<kTmemA, 5, 2, 1>(tmap, p, stream);
+    case 1325: return launch<kTmemA, 5, 3, 1>(tmap, p, stream);
+    case 2125: return launch<kTmemA, 5, 1, 2>(tmap, p, stream);
+    case 2225: return launch<kTmemA, 5, 2, 2>(tmap, p, stream);
+    case 2224: return launch<kTmemA, 4, 2, 2>(tmap, p, stream);
+    default: return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
+  }
+}
+
+}  // namespace gemm
+}  // namespace rl
+
+extern "C" {
+
+int rl_set_gemm_variant(int variant) {
+  const int prev = rl::gemm::g_variant;
+  rl::gemm::g_variant = variant;
+  return prev;
+}
+
+int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                    const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream) {
+  using namespace rl;
+  using namespace rl::gemm;
+  RL_REQUIRE(x && w_native && out, RL_ERR_ARGUMENT, "rl_linear_bfp16: NULL pointer");
+  RL_REQUIRE(M >= 0 && K >= 64 && K % 64 == 0 && N >= 128 && N % 128 == 0, RL_ERR_ARGUMENT,
+             "rl_linear_bfp16: need K %% 64 == 0, N %% 128 == 0 (M=%lld K=%lld N=%lld)", (long long)M, (long long)K,
+             (long long)N);
+  RL_REQUIRE(epilogue == RL_EPI_NONE || epilogue == RL_EPI_BIAS || epilogue == RL_EPI_SWIGLU, RL_ERR_ARGUMENT,
+             "rl_linear_bfp16: bad epilogue %d", epilogue);
+  RL_REQUIRE(epilogue != RL_EPI_BIAS || bias != nullptr, RL_ERR_ARGUMENT, "rl_linear_bfp16: RL_EPI_BIAS needs bias");
+  RL_REQUIRE(out_dtype == RL_BF16 || out_dtype == RL_F32, RL_ERR_ARGUMENT, "rl_linear_bfp16: bad out dtype");
+  RL_REQUIRE(epilogue != RL_EPI_SWIGLU || out_dtype == RL_BF16, RL_ERR_ARGUMENT,
+             "rl_linear_bfp16: SwiGLU writes bf16 (bfp16-rounded) only");
+  RL_REQUIRE(aligned(x, 16) && aligned(w_native, 16) && aligned(out, 16), RL_ERR_ALIGNMENT,
+             "rl_linear_bfp16: x, w_native and out must be 16-byte aligned");
+  RL_REQUIRE(K <= (int64_t)1 << 31 && M < ((int64_t)1 << 31), RL_ERR_ARGUMENT, "rl_linear_bfp16: size too large");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_linear_bfp16: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  EncodeTiledFn enc = encode_tiled();
+  RL_REQUIRE(enc != nullptr, RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled unavailable");
+
+  CUtensorMap tmap;
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {BK, BN};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), gdim, gstride, box,
+                    estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RL_REQUIRE(cr == CUDA_SUCCESS, RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+
+  Params p;
+  p.w9 = w_native;
+  p.bias = (epilogue == RL_EPI_NONE) ? nullptr : bias;
+  p.out = out;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out_f32 = out_dtype == RL_F32;
+  p.epilogue = epilogue;
+  p.num_x_tiles = static_cast<int>((M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(K / BK);
+  return dispatch(g_variant, tmap, p, stream);
+}
+
+}  // extern "C"

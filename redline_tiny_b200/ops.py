@@ -1,0 +1,142 @@
+"""Row-major PyTorch-facing API of the bfp16 hot path (torch CUDA tensors in, torch CUDA tensors out).
+
+torch provides device memory and streams only; every computation is a CUDA kernel of libredline_b200.so, called
+through its C ABI on the current torch stream.
+
+  quantize_bfp16   npu_layouts.to_bfp16 (+ a_layout)             redline/npu_layouts.py:62-88, 18-23
+  dequantize_bfp16 npu_layouts.from_bfp16 (+ a_unlayout)          redline/npu_layouts.py:90-94, 56-60
+  pack_b           pack_weights.pack_b                            redline/pack_weights.py:72-79
+  PackedWeight     a packed B operand resident on the GPU (native tile order)
+  linear_bfp16     gemm() / matmul_vectorized_bfp16 (+ bias)      redline/forward.py:194-197
+  swiglu_up        matmul_swiglu_bfp16 (up GEMM + SwiGLU flush)   kernels/atb3/mm_bfp_swiglu.cc:88-168
+"""
+
+import torch
+
+from . import _lib as L
+
+
+def _stream():
+    return ctypes_ptr(torch.cuda.current_stream().cuda_stream)
+
+
+def ctypes_ptr(v):
+    return None if v is None else int(v)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise ValueError("redline_tiny_b200 ops take CUDA tensors (no CPU path)")
+            if not t.is_contiguous():
+                raise ValueError("tensor must be contiguous")
+
+
+def _dtype_code(t):
+    if t.dtype == torch.float32:
+        return L.RL_F32
+    if t.dtype == torch.bfloat16:
+        return L.RL_BF16
+    raise ValueError(f"unsupported dtype {t.dtype}")
+
+
+_LAYOUTS = {"rowmajor": L.RL_ROWMAJOR, "a_layout": L.RL_A_LAYOUT}
+
+
+def quantize_bfp16(x, layout="rowmajor", want_bytes=True, want_decoded=True):
+    """x (M, K) fp32/bf16 -> (bfp16 bytes uint8 [M*K/8*9] in `layout` order or None,
+    decoded bf16 (M, K) row-major or None)."""
+    _check_cuda(x)
+    M, K = x.shape
+    q = torch.empty(M * K // 8 * 9, dtype=torch.uint8, device=x.device) if want_bytes else None
+    dq = torch.empty((M, K), dtype=torch.bfloat16, device=x.device) if want_decoded else None
+    L.call("rl_quantize_bfp16", _ptr(x), _dtype_code(x), M, K, _LAYOUTS[layout], _ptr(q), _ptr(dq), _stream())
+    return q, dq
+
+
+def dequantize_bfp16(q, M, K, layout="rowmajor", dtype=torch.float32):
+    _check_cuda(q)
+    out = torch.empty((M, K), dtype=dtype, device=q.device)
+    L.call("rl_dequantize_bfp16", _ptr(q), _LAYOUTS[layout], M, K, _ptr(out), _dtype_code(out), _stream())
+    return out
+
+
+def pack_b(B):
+    """B (K, N) fp32/bf16 -> the reference's packed stream to_bfp16(b_layout(B, 64, 128)) as uint8."""
+    _check_cuda(B)
+    K, N = B.shape
+    out = torch.empty(K * N // 8 * 9, dtype=torch.uint8, device=B.device)
+    L.call("rl_pack_b", _ptr(B), _dtype_code(B), K, N, _ptr(out), _stream())
+    return out
+
+
+class PackedWeight:
+    """A B operand (K, N) resident on the GPU in the native tile order (1.125 bytes per weight).
+
+    swiglu=True marks an up matrix with [gate 64 | proj 64] per 128 columns (pack_weights.interleave_up); its
+    rows are arranged for the fused SwiGLU epilogue."""
+
+    def __init__(self, native, K, N, swiglu=False):
+        self.native, self.K, self.N, self.swiglu = native, int(K), int(N), bool(swiglu)
+
+    @classmethod
+    def from_pack_b(cls, packed, K, N, swiglu=False):
+        """The reference's packed bytes (bNN_*.bin contents, as a CUDA uint8 tensor) -> native tiles."""
+        _check_cuda(packed)
+        if packed.numel() != K * N // 8 * 9:
+            raise ValueError(f"packed stream has {packed.numel()} bytes, expected {K * N // 8 * 9}")
+        native = torch.empty_like(packed)
+        L.call("rl_weights_from_pack_b", _ptr(packed), K, N, int(swiglu), _ptr(native), _stream())
+        return cls(native, K, N, swiglu)
+
+    @classmethod
+    def from_float(cls, B, swiglu=False):
+        """Float B (K, N) on the GPU -> native tiles (quantised on the device)."""
+        _check_cuda(B)
+        K, N = B.shape
+        native = torch.empty(K * N // 8 * 9, dtype=torch.uint8, device=B.device)
+        L.call("rl_pack_weights", _ptr(B), _dtype_code(B), K, N, int(swiglu), _ptr(native), _stream())
+        return cls(native, K, N, swiglu)
+
+
+def linear_bfp16(x_dq, w, bias=None, out=None, out_dtype=torch.bfloat16):
+    """C = x_dq @ B (+ bias), x_dq = bf16 (M, K) holding bfp16 values (quantize_bfp16's decoded output)."""
+    _check_cuda(x_dq, w.native, bias, out)
+    if x_dq.dtype != torch.bfloat16:
+        raise ValueError("x must be bf16 holding bfp16-exact values (quantize_bfp16 decoded output)")
+    M, K = x_dq.shape
+    if K != w.K:
+        raise ValueError(f"K mismatch: x has {K}, weight has {w.K}")
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=x_dq.device)
+    epi = L.RL_EPI_BIAS if bias is not None else L.RL_EPI_NONE
+    L.call("rl_linear_bfp16", _ptr(x_dq), M, K, _ptr(w.native), w.N, _ptr(bias), epi, _ptr(out),
+           _dtype_code(out), _stream())
+    return out
+
+
+def swiglu_up(x_dq, w_up, bias=None, out=None):
+    """H = silu(x @ Bgate) * (x @ Bproj), rounded to bfp16 blocks of 8 along F and returned as bf16 (M, F): the
+    down projection's A operand. w_up must be packed with swiglu=True."""
+    _check_cuda(x_dq, w_up.native, bias, out)
+    if not w_up.swiglu:
+        raise ValueError("swiglu_up needs a PackedWeight packed with swiglu=True")
+    M, K = x_dq.shape
+    if out is None:
+        out = torch.empty((M, w_up.N // 2), dtype=torch.bfloat16, device=x_dq.device)
+    L.call("rl_linear_bfp16", _ptr(x_dq), M, K, _ptr(w_up.native), w_up.N, _ptr(bias), L.RL_EPI_SWIGLU,
+           _ptr(out), L.RL_BF16, _stream())
+    return out
+
+
+def set_gemm_variant(v):
+    return L.lib().rl_set_gemm_variant(int(v))
+
+
+def device_status():
+    return L.device_status()

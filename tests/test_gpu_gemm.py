@@ -1,0 +1,128 @@
+"""GPU parity of the packed-weight tcgen05 GEMM (and its SwiGLU epilogue) against the CPU oracle:
+C = from_bfp16(Xq) @ from_bfp16(Wq) (+ bias) in float32 (oracle/bfp16_oracle.linear).
+
+Tolerances (max-rel = max|got - ref| / max|ref|, the statistic of redline/run_ln.py:74-79):
+  fp32 output:  <= 1e-4 against the fp32 oracle (only the accumulation order differs);
+  bf16 output:  <= 2e-3 against the oracle rounded to bf16 - rounding the output to bf16 alone
+                moves a value by up to 2^-8 of max|ref|, so the unrounded oracle is not a fair target;
+  SwiGLU:       <= 2e-3 against the oracle's H rounded to bfp16 (blocks of 8 along F), like the reference's flush."""
+
+import numpy as np
+import pytest
+
+from oracle import bfp16_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = [1, 2]
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    from redline_tiny_b200 import ops
+    assert torch.cuda.is_available()
+    return torch, ops, torch.device("cuda:0")
+
+
+def _case(M, K, N, seed=0, bias=True):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    b = O.bf16_round((rng.standard_normal(N) * 0.01).astype(np.float32)) if bias else None
+    return x, W, b
+
+
+def _run(env, x, W, b, out_dtype, variant, rows=None):
+    torch, ops, dev = env
+    M, K = x.shape
+    N = W.shape[1]
+    prev = ops.set_gemm_variant(variant)
+    try:
+        _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+        w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
+        bt = None if b is None else torch.from_numpy(b).to(dev).to(torch.bfloat16)
+        c = ops.linear_bfp16(dq, w, bias=bt, out_dtype=out_dtype)
+        ops.device_status()
+    finally:
+        ops.set_gemm_variant(prev)
+    got = c.float().cpu().numpy()
+    sel = slice(None) if rows is None else rows
+    _, xd = O.quantize_rows(x[sel])
+    ref = O.linear(xd, O.unpack_b(O.pack_b(W), K, N), b)
+    return got[sel], ref
+
+
+def _diag(got, ref):
+    bad = np.abs(got - ref) > 2e-3 * np.abs(ref).max()
+    if not bad.any():
+        return "ok"
+    r, c = np.nonzero(bad)
+    return (f"{bad.sum()} bad of {bad.size}; rows {np.unique(r)[:16]} ({len(np.unique(r))} distinct), "
+            f"cols {np.unique(c)[:16]} ({len(np.unique(c))} distinct); corr {O.corr(got, ref):.5f}")
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("M,K,N", [(128, 128, 256), (256, 64, 128), (1, 64, 128), (300, 192, 384),
+                                   (512, 4096, 256)])
+def test_linear_small(env, variant, M, K, N):
+    torch = env[0]
+    x, W, b = _case(M, K, N)
+    got, ref = _run(env, x, W, b, torch.float32, variant)
+    err = O.max_rel(got, ref)
+    assert err <= 1e-4, f"max-rel {err:.3e}: {_diag(got, ref)}"
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_linear_bf16_out_no_bias(env, variant):
+    torch = env[0]
+    x, W, _ = _case(384, 256, 512, seed=2, bias=False)
+    got, ref = _run(env, x, W, None, torch.bfloat16, variant)
+    ref = O.bf16_round(ref)
+    err = O.max_rel(got, ref)
+    assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, ref)}"
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_linear_config1_full_size(env, variant):
+    """BASELINE config 1 (DiT FFN up-projection): X[4352, 3072] ~ N(0,1), W[3072, 12288] ~ N(0, 0.02), bias
+    ~ N(0, 0.01), bf16 out. The oracle runs on a sample of 256 rows (every M tile, first and last rows)."""
+    torch = env[0]
+    x, W, b = _case(4352, 3072, 12288, seed=0)
+    rows = np.unique(np.concatenate([np.arange(0, 4352, 17), [0, 255, 256, 4095, 4351]]))
+    got, ref = _run(env, x, W, b, torch.bfloat16, variant, rows=rows)
+    ref = O.bf16_round(ref)
+    err = O.max_rel(got, ref)
+    assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, ref)}"
+
+
+def _swiglu_case(M, K, F, seed=5):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wg = (rng.standard_normal((F, K)) * 0.02).astype(np.float32)
+    wp = (rng.standard_normal((F, K)) * 0.02).astype(np.float32)
+    return x, O.interleave_up(wg, wp)
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("M,K,F", [(128, 128, 128), (300, 256, 256), (512, 4096, 1024)])
+def test_swiglu_up(env, variant, M, K, F):
+    torch, ops, dev = env
+    x, Bup = _swiglu_case(M, K, F)
+    prev = ops.set_gemm_variant(variant)
+    try:
+        _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+        w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(Bup)).to(dev), K, 2 * F, swiglu=True)
+        h = ops.swiglu_up(dq, w)
+        ops.device_status()
+    finally:
+        ops.set_gemm_variant(prev)
+    got = h.float().cpu().numpy()
+    _, xd = O.quantize_rows(x)
+    c = O.linear(xd, O.unpack_b(O.pack_b(Bup), K, 2 * F))
+    href = O.swiglu_from_interleaved(c)
+    _, href_q = O.quantize_rows(href)          # the reference rounds H to bfp16 for the down GEMM
+    err = O.max_rel(got, href_q)
+    assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, href_q)}"
+    # the same bfp16 values almost everywhere (blocks whose rounding sits on a tie can differ by one step)
+    assert np.mean(got == href_q) > 0.99
