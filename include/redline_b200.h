@@ -20,6 +20,7 @@
 #ifndef REDLINE_B200_H
 #define REDLINE_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -112,6 +113,45 @@ int rl_pack_weights(const void* B, int dtype, int64_t K, int64_t N, int swiglu_i
  */
 int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                     const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream);
+
+/*
+ * a9/a13 - the SwiGLU MLP: quantise x (unless x_quantized), H = silu(x @ Bgate) * (x @ Bproj) rounded to bfp16
+ * (the up GEMM with the SwiGLU epilogue), out = H @ Bdown. Replaces the up+SwiGLU / down pair of LM._layer
+ * (redline/vlm_run.py:442-449) and CachedStep.blocks (redline/forward.py:250-251): matmul_swiglu_bfp16
+ * (kernels/atb3/mm_bfp_swiglu.cc:88-168) followed by matmul_vectorized_bfp16.
+ * x: (M, K) RL_BF16 / RL_F32 (x_quantized=1: bf16 already holding bfp16 values); w_up: native (K, F2) packed with
+ * swiglu_interleaved=1, F2 = 2F; w_down: native (F, N); out: (M, N) RL_BF16 or RL_F32.
+ * workspace: caller-owned device scratch of rl_swiglu_mlp_workspace(M, K, F, x_quantized) bytes, 256-byte aligned.
+ */
+size_t rl_swiglu_mlp_workspace(int64_t M, int64_t K, int64_t F, int x_quantized);
+int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up, int64_t F2,
+                  const uint8_t* w_down, int64_t N, void* out, int out_dtype, void* workspace,
+                  size_t workspace_bytes, rl_stream_t stream);
+
+/*
+ * a10 - residual + gate + LayerNorm + modulate between the GEMMs. Replaces the ln_mod artifact
+ * (kernels/glue/ln_mod.cc:92-204, run by forward.py:249, 253, 259) and its numpy model redline/run_ln.py:65-71:
+ *   x' = bf16(x + g * branch)            (float32 arithmetic, one bf16 rounding; bit-exact with run_ln.ln_ref)
+ *   y  = (x' - mean) / sqrt(var + 1e-6) * sc, rounded to bfp16 blocks of 8 along the row.
+ * x, branch (NULL = zero branch): (M, D) bf16 row-major; params: bf16 (2, 2, D) = two rows [g | sc], the layout of
+ * run_ln.ln_params (run_ln.py:38-40); rows r < row_split use parameter row 1 (the reference's S * 128 split).
+ * Outputs (each may be NULL): x_out (M, D) bf16 = x'; y_dq (M, D) bf16 = decoded y (the next GEMM's A operand);
+ * y_q = y's bfp16 bytes, row-major blocks.
+ */
+int rl_ln_mod(const uint16_t* x, const uint16_t* branch, const uint16_t* params, int64_t M, int64_t D,
+              int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream);
+
+/*
+ * a11 - QK-RMSNorm + RoPE. Replaces the qkv_post artifact (kernels/glue/qkv_post.cc:112-178, run by forward.py:246)
+ * and run_glue.rms_rope (redline/run_glue.py:27-37): per token and head, q and k are RMS-normalised over their 128
+ * dims (eps 1e-6), scaled by w_q / w_k, and rotated on adjacent pairs (2i, 2i+1) by the token's (cos, sin).
+ * qkv: (M, 3 * H * 128) bf16 = [q heads | k heads | v heads] (the QKV GEMM output); rope_cs: float32 (M, 64, 2),
+ * the table of host_glue.rope (redline/host_glue.py:68-91); w_q, w_k: float32 [128].
+ * Out: q, k (H, M, 128) bf16; vt (H, 128, ldv) bf16 = V transposed (keys contiguous), columns M..ldv-1 zeroed;
+ * ldv >= M, ldv % 8 == 0.
+ */
+int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
+                uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream);
 
 /* GEMM kernel variant for tests and benchmarks: 0 = default (= 2), 1 = weights decoded into shared memory (MMA A
  * operand from shared memory), 2 = weights decoded into tensor memory (A from TMEM); tuning codes

@@ -3,3 +3,4 @@
 #include "rl_capi.cu"
 #include "rl_codec.cu"
 #include "rl_gemm.cu"
+#include "rl_glue.cu"

@@ -466,3 +466,60 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------
+// SwiGLU MLP: the Qwen3-VL / DiT feed-forward as two packed-weight GEMMs through a caller workspace.
+// ------------------------------------------------------------------------------------------------------------
+namespace rl {
+namespace mlp {
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace layout: [quantised x (M x K bf16) unless x is already bfp16-exact][H (M x F bf16)].
+inline size_t workspace_bytes(int64_t M, int64_t K, int64_t F, int x_quantized) {
+  return (x_quantized ? 0 : align256(static_cast<size_t>(M) * K * 2)) + align256(static_cast<size_t>(M) * F * 2);
+}
+
+int run(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up, int64_t F2,
+        const uint8_t* w_down, int64_t N, void* out, int out_dtype, uint8_t* ws, size_t ws_bytes,
+        cudaStream_t stream) {
+  RL_REQUIRE(x && w_up && w_down && out && ws, RL_ERR_ARGUMENT, "swiglu_mlp: NULL pointer");
+  RL_REQUIRE(F2 % 256 == 0 && K % 64 == 0 && N % 128 == 0 && M >= 0, RL_ERR_ARGUMENT,
+             "swiglu_mlp: need K %% 64 == 0, 2F %% 256 == 0, N %% 128 == 0");
+  RL_REQUIRE(!x_quantized || x_dtype == RL_BF16, RL_ERR_ARGUMENT, "swiglu_mlp: a quantised x must be bf16");
+  const int64_t F = F2 / 2;
+  RL_REQUIRE(ws_bytes >= workspace_bytes(M, K, F, x_quantized), RL_ERR_ARGUMENT,
+             "swiglu_mlp: workspace of %zu bytes, need %zu", ws_bytes, workspace_bytes(M, K, F, x_quantized));
+  RL_REQUIRE(aligned(ws, 256), RL_ERR_ALIGNMENT, "swiglu_mlp: workspace must be 256-byte aligned");
+  if (M == 0) return RL_OK;
+  const uint16_t* xq = static_cast<const uint16_t*>(x);
+  uint8_t* h = ws;
+  if (!x_quantized) {
+    const int st = rl_quantize_bfp16(x, x_dtype, M, K, RL_ROWMAJOR, nullptr, reinterpret_cast<uint16_t*>(ws), stream);
+    if (st != RL_OK) return st;
+    xq = reinterpret_cast<const uint16_t*>(ws);
+    h = ws + align256(static_cast<size_t>(M) * K * 2);
+  }
+  int st = rl_linear_bfp16(xq, M, K, w_up, F2, nullptr, RL_EPI_SWIGLU, h, RL_BF16, stream);
+  if (st != RL_OK) return st;
+  return rl_linear_bfp16(reinterpret_cast<const uint16_t*>(h), M, F, w_down, N, nullptr, RL_EPI_NONE, out,
+                         out_dtype, stream);
+}
+
+}  // namespace mlp
+}  // namespace rl
+
+extern "C" {
+
+size_t rl_swiglu_mlp_workspace(int64_t M, int64_t K, int64_t F, int x_quantized) {
+  return rl::mlp::workspace_bytes(M, K, F, x_quantized);
+}
+
+int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up, int64_t F2,
+                  const uint8_t* w_down, int64_t N, void* out, int out_dtype, void* workspace,
+                  size_t workspace_bytes, rl_stream_t stream) {
+  return rl::mlp::run(x, x_dtype, x_quantized, M, K, w_up, F2, w_down, N, out, out_dtype,
+                      static_cast<uint8_t*>(workspace), workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,228 @@
+// Row kernels between the GEMMs of a DiT block (HBM-bound, one warp per row):
+//   ln_mod   x' = bf16(x + g * branch); y = LayerNorm(x') * sc, rounded to bfp16 along the row (the next GEMM's
+//            A operand). Restates kernels/glue/ln_mod.cc (ln_p1 / ln_fin / ln_p2, lines 92-204) and its numpy model
+//            redline/run_ln.py:65-71, with g = tanh(gate), sc = 1 + scale picked per row from two parameter rows.
+//   qkv_post per head: RMSNorm over 128 dims (eps 1e-6) * w, complex RoPE on adjacent pairs; V passes through and is
+//            written transposed (keys contiguous) for the attention kernel's P.V operand. Restates
+//            kernels/glue/qkv_post.cc (q_post / k_post / v_post, lines 89-178) and redline/run_glue.py:27-37.
+#include "rl_common.cuh"
+#include "rl_host.h"
+
+namespace rl {
+namespace glue {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = float_to_bf16_bits(f[2 * i]) | (float_to_bf16_bits(f[2 * i + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One warp per row; lane l owns the 8-value blocks kb = l, l + 32, ... of the row.
+// params: bf16 [2][2][D] = {row 0: [g | sc], row 1: [g | sc]}; rows < row_split use row 1 (run_ln.py:82-86).
+__global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ br,
+                                                          const uint16_t* __restrict__ params, int64_t M, int64_t D,
+                                                          int64_t row_split, float eps, uint16_t* __restrict__ xo,
+                                                          uint16_t* __restrict__ y_dq, uint8_t* __restrict__ y_q) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t KB = D >> 3;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < M; r += static_cast<int64_t>(gridDim.x) * kWarps) {
+    const uint16_t* prow = params + (r < row_split ? 2 * D : 0);
+    const uint16_t* g = prow;
+    const uint16_t* sc = prow + D;
+    // pass 1: x' = bf16(x + g * branch) in float32 arithmetic (the products are exact: 8-bit x 8-bit significands)
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int64_t kb = lane; kb < KB; kb += 32) {
+      float xf[8], bf[8], gf[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
+      if (br) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(br + r * D) + kb), bf);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bf[i] = 0.0f;
+      }
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = bf16_bits_to_float(float_to_bf16_bits(__fadd_rn(xf[i], __fmul_rn(gf[i], bf[i]))));
+        s1 += v[i];
+        s2 = fmaf(v[i], v[i], s2);
+      }
+      if (xo) reinterpret_cast<uint4*>(xo + r * D)[kb] = pack8(v);
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float mean = s1 / static_cast<float>(D);
+    const float var = fmaxf(s2 / static_cast<float>(D) - mean * mean, 0.0f);
+    const float rstd = 1.0f / sqrtf(var + eps);
+    // pass 2: y = (x' - mean) * rstd * sc, rounded to bfp16 blocks of 8 along the row
+    for (int64_t kb = lane; kb < KB; kb += 32) {
+      float xf[8], bf[8], gf[8], sf[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(sc) + kb), sf);
+      if (br) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(br + r * D) + kb), bf);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bf[i] = 0.0f;
+      }
+      uint32_t bits[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v = bf16_bits_to_float(float_to_bf16_bits(__fadd_rn(xf[i], __fmul_rn(gf[i], bf[i]))));
+        bits[i] = __float_as_uint((v - mean) * rstd * sf[i]);
+      }
+      const uint32_t E = bfp16_block_exponent(bits);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        lo |= (static_cast<uint32_t>(bfp16_quant_one(bits[i], E)) & 0xFFu) << (8 * i);
+        hi |= (static_cast<uint32_t>(bfp16_quant_one(bits[4 + i], E)) & 0xFFu) << (8 * i);
+      }
+      if (y_dq) {
+        uint32_t w[4];
+        bfp16_decode_block(E, lo, hi, w);
+        reinterpret_cast<uint4*>(y_dq + r * D)[kb] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (y_q) {
+        uint8_t* dst = y_q + (r * KB + kb) * 9;
+        dst[0] = static_cast<uint8_t>(E);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dst[1 + i] = static_cast<uint8_t>(lo >> (8 * i));
+          dst[5 + i] = static_cast<uint8_t>(hi >> (8 * i));
+        }
+      }
+    }
+  }
+}
+
+// One warp per (token, head) of Q or K: lane l owns dims 4l..4l+3 (two RoPE pairs).
+// qkv: (M, 3 * H * 128) bf16 = [q heads | k heads | v heads]; cs: (M, 64, 2) float32 (cos, sin) per token and pair;
+// wq, wk: float32 [128]. Out: q, k as (H, M, 128) bf16.
+__global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const uint16_t* __restrict__ qkv,
+                                                                const float* __restrict__ cs,
+                                                                const float* __restrict__ wq,
+                                                                const float* __restrict__ wk, int64_t M, int H,
+                                                                float eps, uint16_t* __restrict__ q,
+                                                                uint16_t* __restrict__ k) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t units = M * H * 2;   // (token, head, q|k)
+  const int64_t ld = static_cast<int64_t>(3) * H * 128;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * kWarps + warp; u < units;
+       u += static_cast<int64_t>(gridDim.x) * kWarps) {
+    const int which = static_cast<int>(u & 1);          // 0 = q, 1 = k
+    const int64_t th = u >> 1;
+    const int64_t m = th / H;
+    const int h = static_cast<int>(th - m * H);
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(qkv + m * ld + (static_cast<int64_t>(which) * H + h) * 128) + lane);
+    float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u), __uint_as_float(raw.y << 16),
+                  __uint_as_float(raw.y & 0xFFFF0000u)};
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
+    const float4 w = __ldg(reinterpret_cast<const float4*>(which ? wk : wq) + lane);
+    const float n0 = v[0] * inv * w.x, n1 = v[1] * inv * w.y, n2 = v[2] * inv * w.z, n3 = v[3] * inv * w.w;
+    const float4 c = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + lane);  // (cos, sin) of pairs 2l, 2l+1
+    const float o0 = n0 * c.x - n1 * c.y, o1 = n0 * c.y + n1 * c.x;
+    const float o2 = n2 * c.z - n3 * c.w, o3 = n2 * c.w + n3 * c.z;
+    uint16_t* dst = (which ? k : q) + (static_cast<int64_t>(h) * M + m) * 128;
+    reinterpret_cast<uint2*>(dst)[lane] = make_uint2(float_to_bf16_bits(o0) | (float_to_bf16_bits(o1) << 16),
+                                                     float_to_bf16_bits(o2) | (float_to_bf16_bits(o3) << 16));
+  }
+}
+
+// V (the third third of qkv) -> vt (H, 128, ldv): 64 tokens x 128 dims per CTA through shared memory.
+__global__ void __launch_bounds__(kThreads) v_transpose_kernel(const uint16_t* __restrict__ qkv, int64_t M, int H,
+                                                               int64_t ldv, uint16_t* __restrict__ vt) {
+  __shared__ uint16_t tile[64][128 + 2];
+  const int64_t ld = static_cast<int64_t>(3) * H * 128;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int h = blockIdx.y;
+  for (int i = threadIdx.x; i < 64 * 64; i += kThreads) {  // 64 tokens x 64 bf16 pairs
+    const int t = i >> 6, d2 = i & 63;
+    const int64_t m = m0 + t;
+    uint32_t w = 0;
+    if (m < M) w = __ldg(reinterpret_cast<const uint32_t*>(qkv + m * ld + (static_cast<int64_t>(2) * H + h) * 128) + d2);
+    tile[t][2 * d2] = static_cast<uint16_t>(w);
+    tile[t][2 * d2 + 1] = static_cast<uint16_t>(w >> 16);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128 * 32; i += kThreads) {  // 128 dims x 32 token pairs
+    const int d = i >> 5, t2 = i & 31;
+    const int64_t m = m0 + 2 * t2;
+    if (m < ldv) {
+      const uint32_t w = static_cast<uint32_t>(tile[2 * t2][d]) | (static_cast<uint32_t>(tile[2 * t2 + 1][d]) << 16);
+      *reinterpret_cast<uint32_t*>(vt + (static_cast<int64_t>(h) * 128 + d) * ldv + m) = w;
+    }
+  }
+}
+
+inline int grid_rows(int64_t units, int per_cta) {
+  const int64_t need = (units + per_cta - 1) / per_cta;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+}  // namespace glue
+}  // namespace rl
+
+extern "C" {
+
+int rl_ln_mod(const uint16_t* x, const uint16_t* branch, const uint16_t* params, int64_t M, int64_t D,
+              int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream) {
+  using namespace rl;
+  RL_REQUIRE(x && params, RL_ERR_ARGUMENT, "rl_ln_mod: NULL pointer");
+  RL_REQUIRE(M >= 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT, "rl_ln_mod: need D %% 8 == 0");
+  RL_REQUIRE(aligned(x, 16) && aligned(branch, 16) && aligned(params, 16) && aligned(x_out, 16) && aligned(y_dq, 16),
+             RL_ERR_ALIGNMENT, "rl_ln_mod: bf16 pointers must be 16-byte aligned");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
+      x, branch, params, M, D, row_split, 1e-6f, x_out, y_dq, y_q);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
+                uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream) {
+  using namespace rl;
+  RL_REQUIRE(qkv && rope_cs && w_q && w_k && q && k && vt, RL_ERR_ARGUMENT, "rl_qkv_post: NULL pointer");
+  RL_REQUIRE(M >= 0 && H > 0 && ldv >= M && ldv % 8 == 0, RL_ERR_ARGUMENT,
+             "rl_qkv_post: need ldv >= M and ldv %% 8 == 0");
+  RL_REQUIRE(aligned(qkv, 16) && aligned(rope_cs, 16) && aligned(w_q, 16) && aligned(w_k, 16) && aligned(q, 16) &&
+                 aligned(k, 16) && aligned(vt, 16),
+             RL_ERR_ALIGNMENT, "rl_qkv_post: pointers must be 16-byte aligned");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_qkv_post: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  glue::qk_norm_rope_kernel<<<glue::grid_rows(M * H * 2, glue::kWarps), glue::kThreads, 0, stream>>>(
+      qkv, rope_cs, w_q, w_k, M, H, 1e-6f, q, k);
+  RL_TRY_CUDA(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>((ldv + 63) / 64), static_cast<unsigned>(H));
+  glue::v_transpose_kernel<<<grid, glue::kThreads, 0, stream>>>(qkv, M, H, ldv, vt);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+}  // extern "C"

@@ -134,6 +134,53 @@ def swiglu_up(x_dq, w_up, bias=None, out=None):
     return out
 
 
+def swiglu_mlp(x, w_up, w_down, out=None, out_dtype=torch.bfloat16, x_quantized=False, workspace=None):
+    """out = (silu(x @ Bgate) * (x @ Bproj)) @ Bdown with bfp16 operands (H rounded to bfp16, as the reference's
+    fused flush does). x (M, K) bf16/fp32 raw activations (or bf16 bfp16-exact values with x_quantized=True)."""
+    _check_cuda(x, w_up.native, w_down.native, out)
+    if not w_up.swiglu:
+        raise ValueError("w_up must be packed with swiglu=True")
+    M, K = x.shape
+    F = w_up.N // 2
+    if w_down.K != F or w_up.K != K:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, up ({w_up.K}, {w_up.N}), down ({w_down.K}, {w_down.N})")
+    if out is None:
+        out = torch.empty((M, w_down.N), dtype=out_dtype, device=x.device)
+    need = L.lib().rl_swiglu_mlp_workspace(M, K, F, int(x_quantized))
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    L.call("rl_swiglu_mlp", _ptr(x), _dtype_code(x), int(x_quantized), M, K, _ptr(w_up.native), w_up.N,
+           _ptr(w_down.native), w_down.N, _ptr(out), _dtype_code(out), _ptr(workspace), workspace.numel(), _stream())
+    return out
+
+
+def ln_mod(x, branch, params, row_split=0, want_x=True, want_y_bytes=False):
+    """x' = bf16(x + g * branch); y = LayerNorm(x') * sc rounded to bfp16 (run_ln.ln_ref).
+    params: bf16 (2, 2, D) = two rows [g | sc] (run_ln.ln_params); rows < row_split use row 1.
+    Returns (x' bf16 or None, y decoded bf16, y bfp16 bytes or None)."""
+    _check_cuda(x, branch, params)
+    M, D = x.shape
+    xo = torch.empty_like(x) if want_x else None
+    y = torch.empty_like(x)
+    yq = torch.empty(M * D // 8 * 9, dtype=torch.uint8, device=x.device) if want_y_bytes else None
+    L.call("rl_ln_mod", _ptr(x), _ptr(branch), _ptr(params), M, D, int(row_split), _ptr(xo), _ptr(y), _ptr(yq),
+           _stream())
+    return xo, y, yq
+
+
+def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None):
+    """QKV GEMM output (M, 3*H*128) -> q, k (H, M, 128) after RMSNorm * w and RoPE; vt (H, 128, ldv) = V^T."""
+    _check_cuda(qkv, rope_cs, w_q, w_k)
+    M = qkv.shape[0]
+    ldv = ldv or (M + 127) // 128 * 128
+    q = torch.empty((heads, M, 128), dtype=torch.bfloat16, device=qkv.device)
+    k = torch.empty_like(q)
+    vt = torch.empty((heads, 128, ldv), dtype=torch.bfloat16, device=qkv.device)
+    L.call("rl_qkv_post", _ptr(qkv), _ptr(rope_cs), _ptr(w_q), _ptr(w_k), M, heads, _ptr(q), _ptr(k), _ptr(vt), ldv,
+           _stream())
+    return q, k, vt
+
+
 def set_gemm_variant(v):
     return L.lib().rl_set_gemm_variant(int(v))
 

@@ -3,8 +3,8 @@ C = from_bfp16(Xq) @ from_bfp16(Wq) (+ bias) in float32 (oracle/bfp16_oracle.lin
 
 Tolerances (max-rel = max|got - ref| / max|ref|, the statistic of redline/run_ln.py:74-79):
   fp32 output:  <= 1e-4 against the fp32 oracle (only the accumulation order differs);
-  bf16 output:  <= 2e-3 against the oracle rounded to bf16 - rounding the output to bf16 alone
-                moves a value by up to 2^-8 of max|ref|, so the unrounded oracle is not a fair target;
+  bf16 output:  <= 2e-3 + 2^-8 against the fp32 oracle: the north-star bound plus the output's own rounding to bf16,
+                which alone moves a value by up to 2^-8 of max|ref|;
   SwiGLU:       <= 2e-3 against the oracle's H rounded to bfp16 (blocks of 8 along F), like the reference's flush."""
 
 import numpy as np
@@ -15,6 +15,7 @@ from oracle import bfp16_oracle as O
 pytestmark = pytest.mark.gpu
 
 VARIANTS = [1, 2]
+BF16_OUT_TOL = 2e-3 + 2.0 ** -8
 
 
 @pytest.fixture(scope="module")
@@ -78,9 +79,8 @@ def test_linear_bf16_out_no_bias(env, variant):
     torch = env[0]
     x, W, _ = _case(384, 256, 512, seed=2, bias=False)
     got, ref = _run(env, x, W, None, torch.bfloat16, variant)
-    ref = O.bf16_round(ref)
     err = O.max_rel(got, ref)
-    assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, ref)}"
+    assert err <= BF16_OUT_TOL, f"max-rel {err:.3e}: {_diag(got, ref)}"
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
@@ -91,9 +91,8 @@ def test_linear_config1_full_size(env, variant):
     x, W, b = _case(4352, 3072, 12288, seed=0)
     rows = np.unique(np.concatenate([np.arange(0, 4352, 17), [0, 255, 256, 4095, 4351]]))
     got, ref = _run(env, x, W, b, torch.bfloat16, variant, rows=rows)
-    ref = O.bf16_round(ref)
     err = O.max_rel(got, ref)
-    assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, ref)}"
+    assert err <= BF16_OUT_TOL, f"max-rel {err:.3e}: {_diag(got, ref)}"
 
 
 def _swiglu_case(M, K, F, seed=5):
