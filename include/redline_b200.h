@@ -129,6 +129,23 @@ int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_
                   size_t workspace_bytes, rl_stream_t stream);
 
 /*
+ * No counterpart in the reference: rl_swiglu_mlp without a caller workspace, for callers that cannot allocate
+ * device memory - a serving process that reserves its whole memory pool at start-up and treats any later
+ * allocation as a failure, or a latency-critical path where cudaMalloc / cudaFree would synchronise the device.
+ * Its scratch is a fixed 32 MiB device array inside this library (rl_swiglu_mlp_noalloc_capacity()), which every
+ * GPU that loads the library holds until the process exits; requests needing more
+ * (rl_swiglu_mlp_workspace(M, K, F, x_quantized) > 32 MiB) return RL_ERR_ARGUMENT. The call allocates nothing.
+ * The first call on each device looks up the array's device address (once, with that device current), so make
+ * that first call before any stream capture. All calls share the one array: calls that overlap on the GPU (e.g. on
+ * two streams) race on it. Nothing in it needs to start zeroed - each call overwrites everything it reads.
+ * Arguments as rl_swiglu_mlp.
+ */
+size_t rl_swiglu_mlp_noalloc_capacity(void);
+int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up,
+                          int64_t F2, const uint8_t* w_down, int64_t N, void* out, int out_dtype,
+                          rl_stream_t stream);
+
+/*
  * a10 - residual + gate + LayerNorm + modulate between the GEMMs. Replaces the ln_mod artifact
  * (kernels/glue/ln_mod.cc:92-204, run by forward.py:249, 253, 259) and its numpy model redline/run_ln.py:65-71:
  *   x' = bf16(x + g * branch)            (float32 arithmetic, one bf16 rounding; bit-exact with run_ln.ln_ref)

@@ -20,6 +20,7 @@
 // The kernel is persistent: one CTA per SM walks tiles (activation-tile fastest, so the CTAs in flight share the
 // same weight columns and the whole X in L2).
 #include <cmath>
+#include <mutex>
 
 #include "rl_common.cuh"
 #include "rl_host.h"
@@ -520,6 +521,69 @@ int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_
                   size_t workspace_bytes, rl_stream_t stream) {
   return rl::mlp::run(x, x_dtype, x_quantized, M, K, w_up, F2, w_down, N, out, out_dtype,
                       static_cast<uint8_t*>(workspace), workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------
+// SwiGLU MLP without any allocation, for callers that cannot allocate device memory: its scratch is a fixed
+// file-scope device array that every GPU loading this library holds until the process exits.
+// ------------------------------------------------------------------------------------------------------------
+namespace rl {
+namespace mlp {
+
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;  // 32 MiB: config 2 (M 512, K 4096, F 12288) needs 16.8 MB
+
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch, looked up once per device (with that device current). In host code the
+// array's name only stands in for the symbol; a kernel must be given this address instead.
+static uint8_t* static_scratch_address(int& status) {
+  constexpr int kMaxDev = 64;
+  static uint8_t* addr[kMaxDev] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    status = fail(RL_ERR_CUDA, "rl_swiglu_mlp_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      status = fail(RL_ERR_CUDA, "rl_swiglu_mlp_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<uint8_t*>(p);
+  }
+  status = RL_OK;
+  return addr[dev];
+}
+
+}  // namespace mlp
+}  // namespace rl
+
+extern "C" {
+
+size_t rl_swiglu_mlp_noalloc_capacity(void) { return rl::mlp::kStaticScratchBytes; }
+
+int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up,
+                          int64_t F2, const uint8_t* w_down, int64_t N, void* out, int out_dtype,
+                          rl_stream_t stream) {
+  using namespace rl;
+  RL_REQUIRE(M >= 0 && K > 0 && F2 > 0 && N > 0, RL_ERR_ARGUMENT, "rl_swiglu_mlp_noalloc: bad shape");
+  const size_t need = mlp::workspace_bytes(M, K, F2 / 2, x_quantized);
+  RL_REQUIRE(need <= mlp::kStaticScratchBytes, RL_ERR_ARGUMENT,
+             "rl_swiglu_mlp_noalloc: M=%lld K=%lld F=%lld needs %zu bytes of scratch, more than the fixed %zu bytes "
+             "(use rl_swiglu_mlp with a caller workspace)",
+             (long long)M, (long long)K, (long long)(F2 / 2), need, mlp::kStaticScratchBytes);
+  int st = RL_OK;
+  uint8_t* scratch = mlp::static_scratch_address(st);
+  if (!scratch) return st;
+  return mlp::run(x, x_dtype, x_quantized, M, K, w_up, F2, w_down, N, out, out_dtype, scratch,
+                  mlp::kStaticScratchBytes, stream);
 }
 
 }  // extern "C"
