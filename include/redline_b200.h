@@ -170,6 +170,20 @@ int rl_ln_mod(const uint16_t* x, const uint16_t* branch, const uint16_t* params,
 int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
                 uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream);
 
+/*
+ * a12 - joint text+image flash attention, head_dim 128, on tcgen05. Replaces the attention artifacts
+ * (kernels/attn/attn_bfp.cc:846-923, run by forward.py:247, 369, 603) and is checked against the float64 softmax of
+ * redline/run_attn.py:203-209 (key-tail mask, run_attn.py:153-155) and run_attn.py:123-126 (per-row key limits).
+ * q: (H, Nq, 128), k: (H, Nk, 128), vt: (H, 128, ldv) bf16 (rl_qkv_post's outputs); keys >= nkv are masked;
+ * row_limit (may be NULL): int32 [Nq], query row r sees keys <= row_limit[r]; logits = (q . k) * scale_log2 in log2
+ * units (log2(e)/sqrt(128) for unscaled q; 1.0 when q already carries it, as the reference's w_q does).
+ * o: (Nq, ldo) bf16, head h at columns [128h, 128h + 128), rounded to bfp16 blocks of 8 (the out-projection's A
+ * operand). Rows with no visible key are zero.
+ */
+int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int64_t Nq,
+                 int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, int64_t ldo,
+                 rl_stream_t stream);
+
 /* GEMM kernel variant for tests and benchmarks: 0 = default (= 2), 1 = weights decoded into shared memory (MMA A
  * operand from shared memory), 2 = weights decoded into tensor memory (A from TMEM); tuning codes
  * 1000*P + 100*G + 10*V + S also select the decode split and the pipeline depth. Returns the previous value. */

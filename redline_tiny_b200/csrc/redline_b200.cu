@@ -4,3 +4,4 @@
 #include "rl_codec.cu"
 #include "rl_gemm.cu"
 #include "rl_glue.cu"
+#include "rl_attn.cu"

@@ -120,18 +120,19 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const T* __restrict_
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads + warp * 32; base < nblocks; base += stride) {
     const int64_t ob = base + lane;
     if (ob < nblocks) {
-      int64_t r, c0;
-      block_coords(layout, ob, K, r, c0);
-      uint32_t b[8];
-      load_block<T>(x + r * K + c0, b);
-      uint32_t E, lo, hi;
-      quant_block(b, E, lo, hi);
-      if (dq) {
-        uint32_t w[4];
-        bfp16_decode_block(E, lo, hi, w);
-        *reinterpret_cast<uint4*>(dq + r * K + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+      // row-major blocks are contiguous: block ob starts at value 8 * ob, no division needed
+      int64_t off = ob * 8;
+      if (layout != RL_ROWMAJOR) {
+        int64_t r, c0;
+        block_coords(layout, ob, K, r, c0);
+        off = r * K + c0;
       }
-      stage_put(stage[warp], lane, E, lo, hi);
+      uint32_t b[8];
+      load_block<T>(x + off, b);
+      uint32_t E, lo, hi, w[4];
+      bfp16_quant_block_fast(b, E, lo, hi, w);
+      if (dq) *reinterpret_cast<uint4*>(dq + off) = make_uint4(w[0], w[1], w[2], w[3]);
+      if (q) stage_put(stage[warp], lane, E, lo, hi);
     }
     if (q) stage_flush(stage[warp], q, base, nblocks, lane);
   }

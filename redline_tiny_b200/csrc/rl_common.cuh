@@ -268,6 +268,15 @@ __device__ __forceinline__ int bfp16_quant_one(uint32_t bits, uint32_t E) {
   return max(-128, min(127, q));
 }
 
+// Quantise one block and decode it again, with float arithmetic (the fast path of the quantiser kernels).
+// E = (max |bits|) >> 23 is the largest exponent field. For E >= 7, s = 2^(133-E) is a normal float and
+// fma(x, s, 1.5 * 2^23) = 1.5 * 2^23 + rint_half_even(x * s) exactly (the product is exact inside the FMA and
+// |x * s| < 256, so the one rounding of the sum is the round-half-even of x * s); the mantissa is clamped to
+// [-128, 127] in float, its low byte read from the bits of m + 1.5 * 2^23, and the decoded value is m * 2^(E-133).
+// Blocks with E < 7 (every value below 2^-120) take the exact integer path above.
+__device__ __forceinline__ void bfp16_quant_block_fast(const uint32_t (&b)[8], uint32_t& E, uint32_t& lo,
+                                                       uint32_t& hi, uint32_t (&dq)[4]);
+
 // 2^(E - 133) as float32 bits (subnormal for E < 7).
 __device__ __forceinline__ float bfp16_scale(uint32_t E) {
   return __uint_as_float(E >= 7u ? ((E - 6u) << 23) : (1u << (E + 16u)));
@@ -306,6 +315,40 @@ __device__ __forceinline__ void bfp16_decode_block(uint32_t E, uint32_t lo, uint
 }
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t h) { return __uint_as_float(h << 16); }
+
+__device__ __forceinline__ void bfp16_quant_block_fast(const uint32_t (&b)[8], uint32_t& E, uint32_t& lo,
+                                                       uint32_t& hi, uint32_t (&dq)[4]) {
+  uint32_t mx = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx = max(mx, b[i] & 0x7FFFFFFFu);
+  E = mx >> 23;
+  if (E >= 7u) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const float s = __uint_as_float((260u - E) << 23);
+    const float inv = __uint_as_float((E - 6u) << 23);
+    uint32_t byte[8];
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = fmaf(__uint_as_float(b[i]), s, kMagic);
+      const float m = fminf(fmaxf(__fsub_rn(y, kMagic), -128.0f), 127.0f);
+      byte[i] = __float_as_uint(__fadd_rn(m, kMagic)) & 0xFFu;
+      v[i] = __fmul_rn(m, inv);
+    }
+    lo = byte[0] | (byte[1] << 8) | (byte[2] << 16) | (byte[3] << 24);
+    hi = byte[4] | (byte[5] << 8) | (byte[6] << 16) | (byte[7] << 24);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dq[i] = __byte_perm(__float_as_uint(v[2 * i]), __float_as_uint(v[2 * i + 1]), 0x7632u);
+  } else {
+    lo = hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      lo |= (static_cast<uint32_t>(bfp16_quant_one(b[i], E)) & 0xFFu) << (8 * i);
+      hi |= (static_cast<uint32_t>(bfp16_quant_one(b[4 + i], E)) & 0xFFu) << (8 * i);
+    }
+    bfp16_decode_block(E, lo, hi, dq);
+  }
+}
 
 // float32 -> bf16 bits, round half to even (finite inputs).
 __device__ __forceinline__ uint32_t float_to_bf16_bits(float f) {

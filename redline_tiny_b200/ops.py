@@ -181,6 +181,26 @@ def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None):
     return q, k, vt
 
 
+def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo=None):
+    """Flash attention per head: q (H, Nq, 128), k (H, Nk, 128), vt (H, 128, ldv) bf16 -> o (Nq, ldo) bf16 with
+    head h at columns 128h.. (rounded to bfp16 along the head dim). scale_log2 defaults to log2(e)/sqrt(128)."""
+    import math
+    _check_cuda(q, k, vt, row_limit, out)
+    H, Nq, _ = q.shape
+    Nk = k.shape[1]
+    ldv = vt.shape[2]
+    nkv = Nk if nkv is None else int(nkv)
+    scale_log2 = math.log2(math.e) / math.sqrt(128) if scale_log2 is None else float(scale_log2)
+    ldo = ldo or H * 128
+    if out is None:
+        out = torch.empty((Nq, ldo), dtype=torch.bfloat16, device=q.device)
+    if row_limit is not None and row_limit.dtype != torch.int32:
+        raise ValueError("row_limit must be int32")
+    L.call("rl_attention", _ptr(q), _ptr(k), _ptr(vt), ldv, H, Nq, Nk, nkv, _ptr(row_limit), scale_log2, _ptr(out),
+           ldo, _stream())
+    return out
+
+
 def set_gemm_variant(v):
     return L.lib().rl_set_gemm_variant(int(v))
 

@@ -1,0 +1,92 @@
+"""GPU parity of the tcgen05 flash-attention kernel against the float64 softmax oracle
+(oracle/bfp16_oracle.attention_f64 = redline/run_attn.py:203-209 and 123-126) on the same bf16 Q/K/V.
+
+The kernel's output is rounded to bfp16 blocks of 8 along the head dim (the out-projection's A operand), so it is
+compared with the oracle rounded the same way: max-rel <= 2e-2 (one bfp16 step is 2^-7 of a block maximum, and P is
+bf16) and correlation > 0.9999 (the reference asks corr > 0.995, run_attn.py:218)."""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import bfp16_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    from redline_tiny_b200 import ops
+    assert torch.cuda.is_available()
+    return torch, ops, torch.device("cuda:0")
+
+
+def _bf16(torch, a, dev):
+    return torch.from_numpy(O.bf16_bits(O.bf16_round(a)).view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+def _run(env, H, Nq, Nk, nkv=None, lim=None, seed=0, heads=None, qscale=1.0):
+    torch, ops, dev = env
+    rng = np.random.default_rng(seed)
+    q = O.bf16_round((rng.standard_normal((H, Nq, 128)) * qscale).astype(np.float32))
+    k = O.bf16_round(rng.standard_normal((H, Nk, 128)).astype(np.float32))
+    v = O.bf16_round(rng.standard_normal((H, Nk, 128)).astype(np.float32))
+    ldv = (Nk + 127) // 128 * 128
+    vt = np.zeros((H, 128, ldv), np.float32)
+    vt[:, :, :Nk] = v.transpose(0, 2, 1)
+    lt = None if lim is None else torch.from_numpy(np.asarray(lim, np.int32)).to(dev)
+    o = ops.attention(_bf16(torch, q, dev), _bf16(torch, k, dev), _bf16(torch, vt, dev), nkv=nkv, row_limit=lt)
+    ops.device_status()
+    o = o.float().cpu().numpy()
+    nkv = Nk if nkv is None else nkv
+    for h in (heads if heads is not None else range(H)):
+        got = o[:, h * 128:(h + 1) * 128]
+        ref = O.attention_f64(q[h], k[h], v[h], row_limit=lim, nkv=nkv)
+        ref = np.nan_to_num(ref)
+        _, refq = O.quantize_rows(ref.astype(np.float32))
+        err, c = O.max_rel(got, refq), O.corr(got, refq)
+        assert err <= 2e-2 and c > 0.9999, f"head {h}: max-rel {err:.3e} corr {c:.6f}"
+    return o
+
+
+@pytest.mark.parametrize("H,N", [(1, 128), (2, 256), (3, 384)])
+def test_attention_square(env, H, N):
+    _run(env, H, N, N, seed=N)
+
+
+def test_attention_ragged_and_key_tail(env):
+    """Nq and Nk not multiples of 128, valid keys < Nk (run_attn.py:153-155: padded keys masked)."""
+    _run(env, 2, 300, 200, nkv=190, seed=3)
+
+
+def test_attention_row_limits(env):
+    """Per-row key limits (run_attn.py:104-106): causal-like rows near the start and rows near the end."""
+    Nq, Nk = 64, 520
+    rng = np.random.default_rng(4)
+    lim = rng.integers(0, Nk - 33, Nq)
+    lim[:8] = np.arange(8)
+    lim[8:40] = Nk - 33 - np.arange(32)[::-1]
+    _run(env, 2, Nq, Nk, lim=lim, seed=4)
+
+
+def test_attention_large_logits_rescale(env):
+    """Large logits force the lazy rescale of O (running maximum rising by more than 8 in log2 units)."""
+    _run(env, 1, 256, 1024, seed=5, qscale=6.0)
+
+
+def test_attention_fully_masked_rows(env):
+    torch = env[0]
+    Nq, Nk = 128, 256
+    lim = np.full(Nq, 100)
+    lim[:5] = -1                                   # these rows see no key at all
+    o = _run(env, 1, Nq, Nk, lim=lim, seed=6, heads=[])
+    assert not o[:5].any()
+    assert np.isfinite(o).all()
+
+
+def test_attention_config3_size(env):
+    """BASELINE config 3 attention: 24 heads x 4352 tokens (256 text + 4096 image), non-causal; heads 0 and 23
+    checked against float64 (run_attn.py:203 checks heads {0, H-1} the same way)."""
+    _run(env, 24, 4352, 4352, seed=7, heads=[0, 23])
