@@ -1,0 +1,195 @@
+"""The DiT denoise step on B200, composed from the hot-path kernels (config 4).
+
+Follows the reference's block sequence (redline/forward.py:240-254, CachedStep.blocks; step structure
+forward.py:396-412, 256-269, 605):
+
+    per block i:  qkv = a @ Wqkv_i -> qkv_post (QK-RMSNorm * w, RoPE) -> attention -> c = o @ Wo_i
+                  x1, a2 = ln_mod(x0, c, p_mlp)          (x1 = x0 + tanh(g1) c; a2 = LN(x1) (1 + s2))
+                  h = SwiGLU(a2 @ Wup_i) -> c = h @ Wdown_i
+                  x0, a = ln_mod(x1, c, p_attn | p_out)  (x0 = x1 + tanh(g2) c; a = LN(x0) (1 + s1 | out scale))
+    per step:     x = [text rows | img_in(latents)], a = LN1 -> 32 blocks -> proj_out on the image rows ->
+                  Euler step on the host.
+
+The adaLN modulation is shared by all blocks ([scale1 | gate1 | scale2 | gate2], host_glue.modulation), with two
+parameter rows: rows below `row_split` (the text prefix) use the t = 0 row, as the reference's ln_mod S split does.
+All activations stay on the GPU in bf16 row-major; every linear is the packed-weight bfp16 GEMM.
+"""
+
+import math
+
+import numpy as np
+import torch
+
+from . import host_glue as HG
+from . import ops
+from . import _lib as L
+
+HEAD_DIM = 128
+C_LOG2 = math.log2(math.e) / math.sqrt(HEAD_DIM)   # folded into w_q as the reference does (forward.py:226-228)
+
+
+class DiTConfig:
+    def __init__(self, hidden=3072, heads=24, ffn=12288, blocks=32, text=256, image=4096, latent_ch=64,
+                 temb_dim=256, grid=(64, 64)):
+        assert hidden == heads * HEAD_DIM and grid[0] * grid[1] == image
+        self.hidden, self.heads, self.ffn, self.blocks = hidden, heads, ffn, blocks
+        self.text, self.image, self.latent_ch, self.temb_dim, self.grid = text, image, latent_ch, temb_dim, grid
+        self.M = text + image
+
+    def flop_per_step(self):
+        M, D, F = self.M, self.hidden, self.ffn
+        per_block = 2 * M * D * 3 * D + 2 * M * D * D + 2 * M * D * 2 * F + 2 * M * F * D + 4 * self.heads * M * M * 128
+        return self.blocks * per_block + 2 * self.image * self.latent_ch * D + 2 * self.image * D * 128
+
+
+def random_weights(cfg, seed=0, device="cuda"):
+    """Random-init weights of the config's architecture (there is no checkpoint): linears N(0, 0.02) as float
+    B = W^T (K, N); QK-norm weights N(1, 0.1); small host weights for the timestep embedding and modulation.
+    Drawn on `device` from a seeded generator (config 4 has 4.8 G weights)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    D, F = cfg.hidden, cfg.ffn
+
+    def randn(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g, device=device) * std).float()
+
+    blocks = []
+    for _ in range(cfg.blocks):
+        blocks.append({
+            "qkv": randn(D, 3 * D), "o": randn(D, D),
+            "gate": randn(F, D), "proj": randn(F, D),           # W (out F, in D), as interleave_up takes them
+            "down": randn(F, D),                                  # B = W_down^T (K = F, N = D)
+            "norm_q": 1 + randn(HEAD_DIM, std=0.1), "norm_k": 1 + randn(HEAD_DIM, std=0.1),
+        })
+    host = {
+        "time_text_embed.timestep_embedder.linear_1.weight": randn(D, cfg.temb_dim).cpu().numpy(),
+        "time_text_embed.timestep_embedder.linear_1.bias": randn(D).cpu().numpy(),
+        "time_text_embed.timestep_embedder.linear_2.weight": randn(D, D).cpu().numpy(),
+        "time_text_embed.timestep_embedder.linear_2.bias": randn(D).cpu().numpy(),
+        "modulation.1.weight": randn(4 * D, D).cpu().numpy(),
+        "norm_out.linear.weight": randn(D, D).cpu().numpy(),
+    }
+    img_in = randn(cfg.latent_ch, D)                      # B = W_img_in^T (64, D)
+    proj_out = torch.zeros(D, 128, device=device)         # B = W_proj_out^T padded to 128 columns
+    proj_out[:, :cfg.latent_ch] = randn(D, cfg.latent_ch)
+    return {"blocks": blocks, "host": host, "img_in": img_in, "proj_out": proj_out}
+
+
+def interleave_up_torch(gate, proj):
+    """[gate 64 | proj 64] per 128 columns of B = [Wgate^T, Wproj^T] (pack_weights.py:82-89)."""
+    F, K = gate.shape
+    B = torch.empty(K, F // 64, 2, 64, dtype=gate.dtype, device=gate.device)
+    B[:, :, 0] = gate.t().reshape(K, F // 64, 64)
+    B[:, :, 1] = proj.t().reshape(K, F // 64, 64)
+    return B.reshape(K, 2 * F)
+
+
+class DiT:
+    """Resident packed weights + preallocated activations for one denoise step of config `cfg` on one GPU."""
+
+    def __init__(self, cfg, weights, device="cuda"):
+        self.cfg = cfg
+        dev = torch.device(device)
+        self.dev = dev
+        D, F, M, H = cfg.hidden, cfg.ffn, cfg.M, cfg.heads
+        pw = ops.PackedWeight.from_float
+        self.blocks = []
+        for b in weights["blocks"]:
+            self.blocks.append({
+                "qkv": pw(b["qkv"].to(dev)), "o": pw(b["o"].to(dev)),
+                "up": pw(interleave_up_torch(b["gate"], b["proj"]).to(dev), swiglu=True),
+                "down": pw(b["down"].to(dev)),
+                "wq": (b["norm_q"] * C_LOG2).to(dev).float().contiguous(),
+                "wk": b["norm_k"].to(dev).float().contiguous(),
+            })
+        self.img_in = pw(weights["img_in"].to(dev))
+        self.proj_out = pw(weights["proj_out"].to(dev))
+        self.host = weights["host"]
+        pad, shapes = HG.joint_layout(np.zeros(cfg.text, bool), n_target=cfg.image, grid=cfg.grid)
+        self.rope_cs = torch.from_numpy(HG.rope(pad, shapes)).to(dev).contiguous()     # (M, 64, 2)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.x = [torch.empty(M, D, **bf) for _ in range(2)]
+        self.emb = torch.empty(M, D, **bf)
+        self.a = torch.empty(M, D, **bf)
+        self.qkv = torch.empty(M, 3 * D, **bf)
+        self.ldv = (M + 127) // 128 * 128
+        self.q = torch.empty(H, M, 128, **bf)
+        self.k = torch.empty(H, M, 128, **bf)
+        self.vt = torch.empty(H, 128, self.ldv, **bf)
+        self.o = torch.empty(M, D, **bf)
+        self.c = torch.empty(M, D, **bf)
+        self.h = torch.empty(M, F, **bf)
+        self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
+        self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
+        self.params = {}
+
+    # --- host glue: per-step adaLN parameters (forward.py:231-238) ---
+    def set_t(self, sigma):
+        cfg, D = self.cfg, self.cfg.hidden
+        te = HG.temb(self.host, HG.model_t(sigma))
+        mod = HG.modulation(self.host, te)
+        out_scale = HG.norm_out_scale(self.host, te)
+        s1, g1, s2, g2 = (mod[:, i * D:(i + 1) * D] for i in range(4))
+
+        def lp(g, sc):
+            p = np.concatenate([np.asarray(g, np.float32), np.asarray(sc, np.float32)], 1).reshape(2, 2, D)
+            return torch.from_numpy(p).to(self.dev).to(torch.bfloat16).contiguous()
+        self.params = {"first": lp(np.ones((2, D)), 1 + s1), "mlp": lp(np.tanh(g1), 1 + s2),
+                       "attn": lp(np.tanh(g2), 1 + s1), "out": lp(np.tanh(g2), 1 + out_scale)}
+
+    def _linear(self, x, w, out, epi=L.RL_EPI_NONE, out_dtype=L.RL_BF16):
+        M, K = x.shape
+        L.call("rl_linear_bfp16", x.data_ptr(), M, K, w.native.data_ptr(), w.N, None, epi, out.data_ptr(), out_dtype,
+               torch.cuda.current_stream().cuda_stream)
+
+    def _ln(self, x, br, params, xo, y):
+        M, D = x.shape
+        L.call("rl_ln_mod", x.data_ptr(), None if br is None else br.data_ptr(), params.data_ptr(), M, D,
+               self.cfg.text, None if xo is None else xo.data_ptr(), y.data_ptr(), None,
+               torch.cuda.current_stream().cuda_stream)
+
+    def embed(self, latents, text_states):
+        """x = [text | img_in(latents)]; a = LN1 (forward.py:396-412 with g = 1 and a zero residual)."""
+        cfg = self.cfg
+        s = torch.cuda.current_stream().cuda_stream
+        lat = latents.to(self.dev, torch.bfloat16).contiguous()
+        L.call("rl_quantize_bfp16", lat.data_ptr(), L.RL_BF16, cfg.image, cfg.latent_ch, L.RL_ROWMAJOR, None,
+               self.lat_dq.data_ptr(), s)
+        self._linear(self.lat_dq, self.img_in, self.emb[cfg.text:])
+        self.emb[:cfg.text].copy_(text_states.to(self.dev, torch.bfloat16))
+        self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
+
+    def block(self, i, last=False):
+        cfg, b = self.cfg, self.blocks[i]
+        s = torch.cuda.current_stream().cuda_stream
+        M, H = cfg.M, cfg.heads
+        self._linear(self.a, b["qkv"], self.qkv)
+        L.call("rl_qkv_post", self.qkv.data_ptr(), self.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(),
+               M, H, self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
+        L.call("rl_attention", self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, H, M, M, M, None,
+               1.0, self.o.data_ptr(), cfg.hidden, s)
+        self._linear(self.o, b["o"], self.c)
+        self._ln(self.x[0], self.c, self.params["mlp"], self.x[1], self.a)
+        self._linear(self.a, b["up"], self.h, epi=L.RL_EPI_SWIGLU)
+        self._linear(self.h, b["down"], self.c)
+        self._ln(self.x[1], self.c, self.params["out" if last else "attn"], self.x[0], self.a)
+
+    def project(self):
+        """proj_out on the image rows of a (= norm_out output) -> velocity (image, 64) float32 (forward.py:261-269)."""
+        cfg = self.cfg
+        self._linear(self.a[cfg.text:], self.proj_out, self.v, out_dtype=L.RL_F32)
+        return self.v[:, :cfg.latent_ch]
+
+    def forward(self, latents, text_states, sigma):
+        """One denoise step's transformer: the velocity for `latents` (image, 64) at noise level `sigma`."""
+        self.set_t(sigma)
+        self.embed(latents, text_states)
+        for i in range(self.cfg.blocks):
+            self.block(i, last=(i == self.cfg.blocks - 1))
+        return self.project()
+
+    def denoise_step(self, latents, text_states, i, sigmas=HG.SIGMAS):
+        """Euler step i of the distilled schedule (forward.py:58-61, 605, 616)."""
+        v = self.forward(latents, text_states, sigmas[i])
+        nxt = sigmas[i + 1] if i + 1 < len(sigmas) else 0.0
+        return latents.to(self.dev, torch.float32) + (nxt - sigmas[i]) * v

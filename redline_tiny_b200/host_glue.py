@@ -62,12 +62,13 @@ def norm_out_scale(w, te):
     return _linear(silu(te), w["norm_out.linear.weight"])
 
 
-def joint_layout(vlm_image_mask, n_target=4096):
+def joint_layout(vlm_image_mask, n_target=4096, grid=(64, 64)):
     """The joint sequence: text positions, image slots expanded to 2x2 latent tokens, then the target's tokens
-    (host_glue.py:59-65). Returns (image_pad_mask, img_shapes)."""
+    (host_glue.py:59-65). Returns (image_pad_mask, img_shapes). `grid` is the latent token grid of each image
+    (64 x 64 at 1024^2, the only size the reference supports; smaller grids serve reduced test configurations)."""
     m = np.concatenate([np.asarray(vlm_image_mask, bool).ravel(), np.ones(n_target // 4, bool)])
     pad = np.repeat(m, np.where(m, 4, 1))
-    return pad, [(1, 64, 64)] * (int(pad.sum()) // n_target)
+    return pad, [(1, grid[0], grid[1])] * (int(pad.sum()) // n_target)
 
 
 def rope(image_pad_mask, img_shapes, axes=(16, 56, 56), theta=10000):

@@ -1,0 +1,75 @@
+"""The DiT denoise step (config 4) on the GPU against the CPU oracle of the same block math (oracle/dit_oracle.py):
+seeded random-init weights of the architecture, latents N(0,1) [image, 64], text states N(0,1).
+
+Bar: the seeded latent after one Euler step reaches cosine >= 0.999 against the oracle; the
+test holds the stricter velocity (the transformer output) to the same cosine, and max-rel <= 5e-2 (every stored
+activation is rounded to bf16 / bfp16 on both sides, and a rounding tie that goes the other way moves one value by one
+bfp16 step)."""
+
+import numpy as np
+import pytest
+
+from oracle import bfp16_oracle as O
+from oracle import dit_oracle as DO
+
+pytestmark = pytest.mark.gpu
+
+
+def _cos(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+def _check(cfg, sigma_index=1, seed=0):
+    import torch
+    from redline_tiny_b200 import dit, host_glue as HG, ops
+
+    w = dit.random_weights(cfg, seed=seed)
+    model = dit.DiT(cfg, w)
+    rng = np.random.default_rng(seed)
+    lat = rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32)
+    txt = rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32)
+    sigma = HG.SIGMAS[sigma_index]
+    v = model.forward(torch.from_numpy(lat), torch.from_numpy(txt), sigma)
+    ops.device_status()
+    v = v.float().cpu().numpy()
+    assert np.isfinite(v).all()
+    ref = DO.forward(cfg, DO.prepare(w), lat, txt, sigma, HG)
+    cv = _cos(v, ref)
+    err = O.max_rel(v, ref)
+    dt = HG.SIGMAS[sigma_index + 1] - sigma
+    cl = _cos(lat + dt * v, lat + dt * ref)
+    assert cv >= 0.999 and cl >= 0.999 and err <= 5e-2, f"velocity cos {cv:.6f} max-rel {err:.3e}; latent cos {cl:.6f}"
+    return cv
+
+
+def test_dit_small():
+    from redline_tiny_b200 import dit
+    cfg = dit.DiTConfig(hidden=256, heads=2, ffn=512, blocks=2, text=64, image=192, grid=(12, 16))
+    _check(cfg)
+
+
+def test_dit_config4_architecture_one_block():
+    """Config 4's architecture (hidden 3072, 24 x 128 heads, SwiGLU FFN 12288, 256 text + 4096 image tokens) with one
+    of its 32 blocks, so the CPU oracle finishes in under a minute; the full 32-block step runs below and in
+    bench.py."""
+    from redline_tiny_b200 import dit
+    cfg = dit.DiTConfig(blocks=1)
+    _check(cfg, sigma_index=3, seed=1)
+
+
+def test_dit_full_step_runs():
+    """All 32 blocks of config 4 on the GPU: finite velocity of the expected shape (size-independent check; the
+    block math is pinned by the two tests above)."""
+    import torch
+    from redline_tiny_b200 import dit, ops
+    cfg = dit.DiTConfig()
+    model = dit.DiT(cfg, dit.random_weights(cfg, seed=2))
+    rng = np.random.default_rng(2)
+    lat = torch.from_numpy(rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32))
+    txt = torch.from_numpy(rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32))
+    out = model.denoise_step(lat, txt, 0)
+    ops.device_status()
+    out = out.cpu().numpy()
+    assert out.shape == (cfg.image, cfg.latent_ch) and np.isfinite(out).all()
+    assert 0.1 < out.std() < 10
