@@ -63,6 +63,20 @@ struct Params {
   int nblk;
 };
 
+// 2^x with the hardware approximation (MUFU.EX2); exp2(-inf) = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two floats -> bf16x2 (round to nearest even), low half = a.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
@@ -211,15 +225,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         RL_TMEM_LD32(ta + 96, s3);
         tmem_ld_wait_regs(s);
       }
-      // logits in log2 units, masked: key j*128 + c is visible iff key <= lim (lim < nkv)
+      // logits in log2 units, masked: key j*128 + c is visible iff key <= lim (lim < nkv); the maximum is taken on
+      // the raw scores (scale_log2 > 0), masked entries set to -inf only in blocks that reach past lim
       const int64_t key0 = static_cast<int64_t>(j) * BKV;
       float mx = -INFINITY;
+      if (key0 + BKV - 1 <= lim) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float x = (key0 + c <= lim) ? __uint_as_float(s[c]) * p.scale_log2 : -INFINITY;
-        s[c] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          if (key0 + c > lim) s[c] = 0xFF800000u;  // -inf
+          mx = fmaxf(mx, __uint_as_float(s[c]));
+        }
       }
+      mx *= p.scale_log2;
       const bool raise = mx > m_run + kTau;      // true on the first block with any visible key
       float alpha = 1.0f;
       if (raise) {
@@ -242,17 +262,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_wait_regs(o);
         }
       }
-      // P = exp2(logit - m_run) as bf16, summed as rounded (what P.V accumulates), written over S
-      const bool dead = (m_run == -INFINITY);
-      float lsum = 0.0f;
+      // P = 2^(logit - m_run) with the hardware exp2 (P is stored as bf16 anyway), written over S
       uint32_t pk[64];
+      float lsum = 0.0f;
+      if (m_run == -INFINITY) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = dead ? 0.0f : exp2f(__uint_as_float(s[2 * c]) - m_run);
-        const float p1 = dead ? 0.0f : exp2f(__uint_as_float(s[2 * c + 1]) - m_run);
-        const uint32_t b0 = float_to_bf16_bits(p0), b1 = float_to_bf16_bits(p1);
-        lsum += bf16_bits_to_float(b0) + bf16_bits_to_float(b1);
-        pk[c] = b0 | (b1 << 16);
+        for (int c = 0; c < 64; ++c) pk[c] = 0u;
+      } else {
+        const float nm = -m_run, sc = p.scale_log2;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), sc, nm));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), sc, nm));
+          lsum += p0 + p1;
+          pk[c] = pack_bf16x2(p0, p1);
+        }
       }
       l_run += lsum;
       {

@@ -36,7 +36,8 @@ constexpr int X_BYTES = BN * BK * 2;    // 32768
 constexpr int WE_BYTES = BM * BK * 2;   // 16384 (decoded weights, shared-memory variant)
 constexpr int W9_BYTES = 9216;          // one native weight tile
 constexpr int kChunk = 16;              // epilogue: D columns (activation rows) per tcgen05.ld
-constexpr int kEpiStageBytes = kChunk * 32 * 4;  // per epilogue warp: 16 rows x 32 columns x fp32
+constexpr int kSwStride = 36;           // SwiGLU staging row stride (floats): 16-byte rows without bank conflicts
+constexpr int kEpiStageBytes = kChunk * kSwStride * 4;  // per epilogue warp: 16 rows x 32 columns x fp32 (+pad)
 
 enum Variant { kSmemA = 1, kTmemA = 2 };
 
@@ -84,39 +85,36 @@ struct Barriers {
   int abort;
 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// silu with the fast intrinsics (error ~1e-6 relative, far below the bfp16 step the result is rounded to)
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // Epilogue of one 16-column chunk of D (16 activation rows x this warp's 32 weight columns): bias, SwiGLU or plain
 // conversion, transposed through the warp's staging buffer into row-major global memory.
 __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&r)[kChunk], uint8_t* st, int lane,
                                                int q, int wt, int64_t x0, float bias_v) {
   if (p.epilogue == RL_EPI_SWIGLU) {
-    // lanes 0-15: gate of units 16q + lane; lanes 16-31: proj of the same units
-    uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
+    // lanes 0-15 hold the gate of units 16q + lane, lanes 16-31 the proj of the same units. Stage the chunk
+    // (16 rows x 32 values, row stride 36 floats: conflict-free both ways), then lane (row = lane & 15,
+    // half = lane >> 4) owns 8 consecutive units of one row - one bfp16 block, so the block maximum is local.
+    float* s32 = reinterpret_cast<float*>(st);
 #pragma unroll
-    for (int j = 0; j < kChunk; ++j) {
-      const float v = __uint_as_float(r[j]) + bias_v;
-      const float pv = __shfl_down_sync(0xffffffffu, v, 16);
-      const float h = silu_f(v) * pv;
-      // round h to bfp16 with blocks of 8 consecutive units (8 lanes), as the down GEMM's A operand
-      const uint32_t hb = __float_as_uint(h);
-      uint32_t e = (hb >> 23) & 0xFFu;
-      e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
-      e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
-      e = max(e, __shfl_xor_sync(0xffffffffu, e, 4));
-      const int m = bfp16_quant_one(hb, e);
-      const float dq = __fmul_rn(static_cast<float>(m), bfp16_scale(e));
-      if (lane < 16) s16[j * 16 + lane] = static_cast<uint16_t>(__float_as_uint(dq) >> 16);
-    }
+    for (int j = 0; j < kChunk; ++j) s32[j * kSwStride + lane] = __uint_as_float(r[j]) + bias_v;
     __syncwarp();
-    // 16 rows x 16 units bf16 = 32 B per row: 32 pieces of 16 bytes, one per lane
+    const int rr = lane & 15, part = lane >> 4;
+    const float4* rowp = reinterpret_cast<const float4*>(s32 + rr * kSwStride + 8 * part);
+    const float4 g0 = rowp[0], g1 = rowp[1], p0 = rowp[4], p1 = rowp[5];   // proj is 16 floats to the right
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    uint32_t hb[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hb[i] = __float_as_uint(silu_f(gv[i]) * pv[i]);
+    uint32_t E, lo, hi, w[4];
+    bfp16_quant_block_fast(hb, E, lo, hi, w);
     const int64_t Nout = p.N / 2;
-    uint16_t* outp = static_cast<uint16_t*>(p.out);
-    const int rr = lane >> 1, part = lane & 1;
     const int64_t xr = x0 + rr;
     if (xr < p.M)
-      *reinterpret_cast<uint4*>(outp + xr * Nout + static_cast<int64_t>(wt) * 64 + 16 * q + part * 8) =
-          reinterpret_cast<const uint4*>(s16 + rr * 16)[part];
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + xr * Nout + static_cast<int64_t>(wt) * 64 + 16 * q +
+                                8 * part) = make_uint4(w[0], w[1], w[2], w[3]);
     __syncwarp();
   } else if (!p.out_f32) {
     uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
