@@ -39,6 +39,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-rows", type=int, default=128, help="reference arm: X rows per step (bounded sample)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 2-5 measurements")
     return ap.parse_args()
 
 
@@ -188,6 +189,93 @@ def run_reference(args, ws, rank):
     print(json.dumps(out), flush=True)
 
 
+def _event_ms(fn, n, w, stream):
+    import torch
+    for _ in range(w):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def measure_configs(dev, stream, ws, seed):
+    """The other BASELINE configs on this GPU (every rank runs its own copy: data-parallel), CUDA-event timed.
+    Inputs are seeded synthetic tensors of the configs' shapes; weights N(0, 0.02)."""
+    import math
+    import torch
+    from redline_tiny_b200 import dit, ops
+    from redline_tiny_b200 import _lib as L
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = {}
+    # config 5: the GEMM M sweep at K=3072, N=12288 (bias, bf16 out); inputs rotate over 2 sets
+    K5, N5 = 3072, 12288
+    ws5 = [ops.PackedWeight.from_float(torch.randn((K5, N5), generator=g, device=dev) * 0.02) for _ in range(2)]
+    bias = (torch.randn((N5,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+    sweep = {}
+    for Ms in (256, 1024, 4352, 17408):
+        xs = [ops.quantize_bfp16(torch.randn((Ms, K5), generator=g, device=dev).to(torch.bfloat16),
+                                 want_bytes=False)[1] for _ in range(2)]
+        c = torch.empty((Ms, N5), dtype=torch.bfloat16, device=dev)
+        it = [0]
+
+        def f():
+            i = it[0] = it[0] + 1
+            L.call("rl_linear_bfp16", xs[i % 2].data_ptr(), Ms, K5, ws5[i % 2].native.data_ptr(), N5, bias.data_ptr(),
+                   L.RL_EPI_BIAS, c.data_ptr(), L.RL_BF16, stream.cuda_stream)
+        ms = _event_ms(f, 20, 3, stream)
+        sweep[str(Ms)] = {"ms": ms, "TFLOP/s": 2.0 * Ms * N5 * K5 / (ms * 1e-3) / 1e12}
+        del xs, c
+    out["C5_gemm_sweep_K3072_N12288"] = sweep
+    del ws5
+    # config 2: Qwen3-VL SwiGLU MLP, X[512, 4096] -> gate/up [4096, 12288] -> down [12288, 4096]
+    M2, K2, F2, N2 = 512, 4096, 12288, 4096
+    wu = ops.PackedWeight.from_float(torch.randn((K2, 2 * F2), generator=g, device=dev) * 0.02, swiglu=True)
+    wd = ops.PackedWeight.from_float(torch.randn((F2, N2), generator=g, device=dev) * 0.02)
+    x2 = torch.randn((M2, K2), generator=g, device=dev).to(torch.bfloat16)
+    o2 = torch.empty((M2, N2), dtype=torch.bfloat16, device=dev)
+    wsp = torch.empty(L.lib().rl_swiglu_mlp_workspace(M2, K2, F2, 0), dtype=torch.uint8, device=dev)
+    ms = _event_ms(lambda: ops.swiglu_mlp(x2, wu, wd, out=o2, workspace=wsp), 20, 3, stream)
+    fl = 2.0 * M2 * K2 * 2 * F2 + 2.0 * M2 * F2 * N2
+    out["C2_swiglu_mlp"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "weights_MB": 169.87}
+    del wu, wd, wsp
+    # configs 3 and 4: the DiT (hidden 3072, 24 x 128 heads, FFN 12288, 256 text + 4096 image tokens)
+    cfg = dit.DiTConfig()
+    model = dit.DiT(cfg, dit.random_weights(cfg, seed=seed))
+    lat = torch.randn((cfg.image, cfg.latent_ch), generator=g, device=dev)
+    txt = torch.randn((cfg.text, cfg.hidden), generator=g, device=dev)
+    model.set_t(0.5)
+    model.embed(lat, txt)
+    b0 = model.blocks[0]
+
+    def sublayer():   # config 3: the joint-attention sublayer
+        model._linear(model.a, b0["qkv"], model.qkv)
+        L.call("rl_qkv_post", model.qkv.data_ptr(), model.rope_cs.data_ptr(), b0["wq"].data_ptr(),
+               b0["wk"].data_ptr(), cfg.M, cfg.heads, model.q.data_ptr(), model.k.data_ptr(), model.vt.data_ptr(),
+               model.ldv, stream.cuda_stream)
+        L.call("rl_attention", model.q.data_ptr(), model.k.data_ptr(), model.vt.data_ptr(), model.ldv, cfg.heads,
+               cfg.M, cfg.M, cfg.M, None, 1.0, model.o.data_ptr(), cfg.hidden, stream.cuda_stream)
+        model._linear(model.o, b0["o"], model.c)
+    ms = _event_ms(sublayer, 10, 3, stream)
+    M, D = cfg.M, cfg.hidden
+    fl = 2.0 * M * D * 3 * D + 2.0 * M * D * D + 4.0 * cfg.heads * M * M * 128
+    out["C3_joint_attention_sublayer"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "GFLOP": fl / 1e9}
+
+    def step():       # config 4: one full denoise step (embed, 32 blocks, proj_out, Euler on the GPU)
+        model.denoise_step(lat, txt, 3)
+    ms = _event_ms(step, 3, 2, stream)
+    out["C4_dit_step"] = {"ms": ms, "TFLOP/s": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
+                          "TFLOP_per_step": cfg.flop_per_step() / 1e12, "weights_GB": 5.44}
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, ws, rank, local):
     import numpy as np
     import torch
@@ -284,6 +372,26 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
 
+    extras = measure_configs(dev, stream, ws, seed=100 + rank) if not args.no_extras else {}
+    if ws > 1 and extras:   # max over ranks of every timing
+        flat = [v["ms"] for v in extras["C5_gemm_sweep_K3072_N12288"].values()] + [
+            extras[k]["ms"] for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step")]
+        tt = torch.tensor(flat, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        mx = tt.tolist()
+        for i, key in enumerate(extras["C5_gemm_sweep_K3072_N12288"]):
+            e = extras["C5_gemm_sweep_K3072_N12288"][key]
+            e["TFLOP/s"] *= e["ms"] / mx[i]
+            e["ms"] = mx[i]
+        for j, key in enumerate(("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step")):
+            e = extras[key]
+            e["TFLOP/s"] *= e["ms"] / mx[4 + j]
+            e["ms"] = mx[4 + j]
+    if extras:
+        extras["C4_dit_step"]["images_per_s_all_gpus"] = ws * 1e3 / extras["C4_dit_step"]["ms"]
+        extras["note"] = ("per-GPU timings (max over ranks); each GPU runs its own copy (data-parallel); "
+                          "TFLOP/s per GPU")
+
     if rank != 0:
         if ws > 1:
             dist.barrier()
@@ -309,6 +417,7 @@ def run_ours(args, ws, rank, local):
            "e2e": {"value": FLOP * e2e_steps * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
            "gpu_launches": 2 * args.steps,
+           "configs": extras,
            "kernel_ms": {"bfp16_linear": gemm_ms, "quantize+linear": ms / args.steps}}
     if ws == 1 and not args.no_cpu_baseline:
         tf, dt, cores = cpu_baseline_sample(M)
