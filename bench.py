@@ -117,14 +117,19 @@ class ClockSampler:
 
 
 def dist_init(args):
+    os.environ.setdefault("NCCL_DEBUG", "WARN")   # rank 0's stdout carries exactly one JSON line
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if ws > 1:
         import datetime
+        import torch
         import torch.distributed as dist
+        kw = {"device_id": torch.device("cuda", local)} if args.impl == "ours" else {}
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
         dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
-                                timeout=datetime.timedelta(seconds=120))
+                                timeout=datetime.timedelta(seconds=120), **kw)
     return ws, rank, local
 
 
@@ -273,6 +278,22 @@ def measure_configs(dev, stream, ws, seed):
                           "TFLOP_per_step": cfg.flop_per_step() / 1e12, "weights_GB": 5.44}
     del model
     torch.cuda.empty_cache()
+    if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1 (NCCL all-reduce of fp32 partials)
+        import torch.distributed as dist
+        rank = dist.get_rank()
+        w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
+        tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD))
+        del w
+        torch.cuda.empty_cache()
+        lat1 = torch.randn((cfg.image, cfg.latent_ch), generator=torch.Generator(device=dev).manual_seed(7),
+                           device=dev)
+        txt1 = torch.randn((cfg.text, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(8), device=dev)
+        dist.barrier()
+        ms = _event_ms(lambda: tp_model.denoise_step(lat1, txt1, 3), 3, 2, stream)
+        out[f"C4_dit_step_tp{ws}"] = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
+                                      "all_reduce_per_step": 2 * cfg.blocks, "all_reduce_bytes": cfg.M * cfg.hidden * 4}
+        del tp_model
+        torch.cuda.empty_cache()
     return out
 
 
@@ -375,7 +396,8 @@ def run_ours(args, ws, rank, local):
     extras = measure_configs(dev, stream, ws, seed=100 + rank) if not args.no_extras else {}
     if ws > 1 and extras:   # max over ranks of every timing
         flat = [v["ms"] for v in extras["C5_gemm_sweep_K3072_N12288"].values()] + [
-            extras[k]["ms"] for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step")]
+            extras[k]["ms"] for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step",
+                                      f"C4_dit_step_tp{ws}")]
         tt = torch.tensor(flat, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         mx = tt.tolist()
@@ -383,9 +405,11 @@ def run_ours(args, ws, rank, local):
             e = extras["C5_gemm_sweep_K3072_N12288"][key]
             e["TFLOP/s"] *= e["ms"] / mx[i]
             e["ms"] = mx[i]
-        for j, key in enumerate(("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step")):
+        for j, key in enumerate(("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step",
+                                 f"C4_dit_step_tp{ws}")):
             e = extras[key]
-            e["TFLOP/s"] *= e["ms"] / mx[4 + j]
+            rate = "TFLOP/s_all_gpus" if key.startswith("C4_dit_step_tp") else "TFLOP/s"
+            e[rate] *= e["ms"] / mx[4 + j]
             e["ms"] = mx[4 + j]
     if extras:
         extras["C4_dit_step"]["images_per_s_all_gpus"] = ws * 1e3 / extras["C4_dit_step"]["ms"]

@@ -150,12 +150,13 @@ int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M
  * (kernels/glue/ln_mod.cc:92-204, run by forward.py:249, 253, 259) and its numpy model redline/run_ln.py:65-71:
  *   x' = bf16(x + g * branch)            (float32 arithmetic, one bf16 rounding; bit-exact with run_ln.ln_ref)
  *   y  = (x' - mean) / sqrt(var + 1e-6) * sc, rounded to bfp16 blocks of 8 along the row.
- * x, branch (NULL = zero branch): (M, D) bf16 row-major; params: bf16 (2, 2, D) = two rows [g | sc], the layout of
+ * x: (M, D) bf16 row-major; branch (NULL = zero branch): (M, D) row-major, RL_BF16, or RL_F32 (e.g. the sum of
+ * tensor-parallel partial GEMM outputs; rounded to bf16 on load); params: bf16 (2, 2, D) = two rows [g | sc], the layout of
  * run_ln.ln_params (run_ln.py:38-40); rows r < row_split use parameter row 1 (the reference's S * 128 split).
  * Outputs (each may be NULL): x_out (M, D) bf16 = x'; y_dq (M, D) bf16 = decoded y (the next GEMM's A operand);
  * y_q = y's bfp16 bytes, row-major blocks.
  */
-int rl_ln_mod(const uint16_t* x, const uint16_t* branch, const uint16_t* params, int64_t M, int64_t D,
+int rl_ln_mod(const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream);
 
 /*

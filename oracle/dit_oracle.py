@@ -56,8 +56,11 @@ def _ln(x, br, p, split):
     return xp, O.quantize_rows(y.astype(np.float32))[1]
 
 
-def forward(cfg, prep, latents, text_states, sigma, host_glue):
-    D, H, M, T = cfg.hidden, cfg.heads, cfg.M, cfg.text
+def forward(cfg, prep, latents, text_states, sigma, host_glue, reduce=None):
+    """The step's velocity. With tensor-parallel shards in `prep`, `reduce` sums a partial (M, D) float32
+    projection output over the ranks (an all-reduce) before it is rounded to bf16."""
+    D, M, T = cfg.hidden, cfg.M, cfg.text
+    reduce = reduce or (lambda c: c)
     te = host_glue.temb(prep["host"], host_glue.model_t(sigma))
     mod = host_glue.modulation(prep["host"], te)
     out_scale = host_glue.norm_out_scale(prep["host"], te)
@@ -77,8 +80,9 @@ def forward(cfg, prep, latents, text_states, sigma, host_glue):
     emb[T:] = O.bf16_round(O.linear(lat, prep["img_in"]))
     x0, a = _ln(emb, np.zeros_like(emb), p_first, T)
     for i, b in enumerate(prep["blocks"]):
+        H = b["qkv"].shape[1] // (3 * HEAD_DIM)       # heads on this rank
         qkv = O.bf16_round(O.linear(a, b["qkv"]))
-        o = np.empty((M, D), np.float32)
+        o = np.empty((M, H * HEAD_DIM), np.float32)
         for h in range(H):
             q = O.bf16_round(O.rms_rope(qkv[:, h * 128:(h + 1) * 128], b["wq"], cos, sin))
             k = O.bf16_round(O.rms_rope(qkv[:, (H + h) * 128:(H + h + 1) * 128], b["wk"], cos, sin))
@@ -87,10 +91,10 @@ def forward(cfg, prep, latents, text_states, sigma, host_glue):
             o[:, h * 128:(h + 1) * 128] = O.attention_f64(q * np.float32(math.sqrt(HEAD_DIM) / math.log2(math.e)),
                                                           k, v)
         o = O.quantize_rows(o)[1]
-        c = O.bf16_round(O.linear(o, b["o"]))
+        c = O.bf16_round(reduce(O.linear(o, b["o"])))
         x1, a = _ln(x0, c, p_mlp, T)
         hsw = O.quantize_rows(O.swiglu_from_interleaved(O.linear(a, b["up"])))[1]
-        c = O.bf16_round(O.linear(hsw, b["down"]))
+        c = O.bf16_round(reduce(O.linear(hsw, b["down"])))
         x0, a = _ln(x1, c, p_out if i == len(prep["blocks"]) - 1 else p_attn, T)
     v = O.linear(a[T:], prep["proj_out"])
     return v[:, :cfg.latent_ch]

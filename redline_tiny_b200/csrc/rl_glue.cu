@@ -38,8 +38,24 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 
 // One warp per row; lane l owns the 8-value blocks kb = l, l + 32, ... of the row.
 // params: bf16 [2][2][D] = {row 0: [g | sc], row 1: [g | sc]}; rows < row_split use row 1 (run_ln.py:82-86).
+__device__ __forceinline__ void load_branch(const void* br, int br_f32, int64_t r, int64_t D, int64_t kb,
+                                            float (&f)[8]) {
+  if (!br) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = 0.0f;
+  } else if (br_f32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(br) + r * D) + 2 * kb;
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(br) + r * D) + kb), f);
+  }
+}
+
+// The branch is bf16, or fp32 (the sum of tensor-parallel partial GEMM outputs), rounded to bf16 on load in both
+// cases: x' = bf16(x + g * bf16(branch)).
 __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __restrict__ x,
-                                                          const uint16_t* __restrict__ br,
+                                                          const void* __restrict__ br, int br_f32,
                                                           const uint16_t* __restrict__ params, int64_t M, int64_t D,
                                                           int64_t row_split, float eps, uint16_t* __restrict__ xo,
                                                           uint16_t* __restrict__ y_dq, uint8_t* __restrict__ y_q) {
@@ -55,11 +71,10 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
       float xf[8], bf[8], gf[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
       unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
-      if (br) {
-        unpack8(__ldg(reinterpret_cast<const uint4*>(br + r * D) + kb), bf);
-      } else {
+      load_branch(br, br_f32, r, D, kb, bf);
+      if (br_f32) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bf[i] = 0.0f;
+        for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
       }
       float v[8];
 #pragma unroll
@@ -81,11 +96,10 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
       unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
       unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
       unpack8(__ldg(reinterpret_cast<const uint4*>(sc) + kb), sf);
-      if (br) {
-        unpack8(__ldg(reinterpret_cast<const uint4*>(br + r * D) + kb), bf);
-      } else {
+      load_branch(br, br_f32, r, D, kb, bf);
+      if (br_f32) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bf[i] = 0.0f;
+        for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
       }
       uint32_t bits[8];
 #pragma unroll
@@ -190,17 +204,18 @@ inline int grid_rows(int64_t units, int per_cta) {
 
 extern "C" {
 
-int rl_ln_mod(const uint16_t* x, const uint16_t* branch, const uint16_t* params, int64_t M, int64_t D,
+int rl_ln_mod(const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream) {
   using namespace rl;
   RL_REQUIRE(x && params, RL_ERR_ARGUMENT, "rl_ln_mod: NULL pointer");
   RL_REQUIRE(M >= 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT, "rl_ln_mod: need D %% 8 == 0");
+  RL_REQUIRE(branch_dtype == RL_BF16 || branch_dtype == RL_F32, RL_ERR_ARGUMENT, "rl_ln_mod: bad branch dtype");
   RL_REQUIRE(aligned(x, 16) && aligned(branch, 16) && aligned(params, 16) && aligned(x_out, 16) && aligned(y_dq, 16),
              RL_ERR_ALIGNMENT, "rl_ln_mod: bf16 pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod: needs an sm_100 device");
   if (M == 0) return RL_OK;
   glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      x, branch, params, M, D, row_split, 1e-6f, x_out, y_dq, y_q);
+      x, branch, branch_dtype == RL_F32 ? 1 : 0, params, M, D, row_split, 1e-6f, x_out, y_dq, y_q);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

@@ -75,6 +75,28 @@ def random_weights(cfg, seed=0, device="cuda"):
     return {"blocks": blocks, "host": host, "img_in": img_in, "proj_out": proj_out}
 
 
+def shard_weights(weights, cfg, rank, world):
+    """Tensor-parallel shard `rank` of `world` (SURVEY 8e-ii layout): QKV columns and out-projection rows of this
+    rank's heads (each head's q, k and v stay together), gate / proj units and down-projection rows of this rank's
+    FFN units (interleaved 128-column tiles stay whole). Norm and host weights are replicated."""
+    H, F, D = cfg.heads, cfg.ffn, cfg.hidden
+    assert H % world == 0 and F % (64 * world) == 0, "heads and FFN units must split evenly (units by 64)"
+    hl, fl = H // world, F // world
+    c0, c1 = rank * hl * HEAD_DIM, (rank + 1) * hl * HEAD_DIM
+    blocks = []
+    for b in weights["blocks"]:
+        qkv = b["qkv"]
+        blocks.append({
+            "qkv": torch.cat([qkv[:, c0:c1], qkv[:, D + c0:D + c1], qkv[:, 2 * D + c0:2 * D + c1]], 1).contiguous(),
+            "o": b["o"][c0:c1].contiguous(),
+            "gate": b["gate"][rank * fl:(rank + 1) * fl].contiguous(),
+            "proj": b["proj"][rank * fl:(rank + 1) * fl].contiguous(),
+            "down": b["down"][rank * fl:(rank + 1) * fl].contiguous(),
+            "norm_q": b["norm_q"], "norm_k": b["norm_k"],
+        })
+    return {"blocks": blocks, "host": weights["host"], "img_in": weights["img_in"], "proj_out": weights["proj_out"]}
+
+
 def interleave_up_torch(gate, proj):
     """[gate 64 | proj 64] per 128 columns of B = [Wgate^T, Wproj^T] (pack_weights.py:82-89)."""
     F, K = gate.shape
@@ -85,13 +107,21 @@ def interleave_up_torch(gate, proj):
 
 
 class DiT:
-    """Resident packed weights + preallocated activations for one denoise step of config `cfg` on one GPU."""
+    """Resident packed weights + preallocated activations for one denoise step of config `cfg` on one GPU.
 
-    def __init__(self, cfg, weights, device="cuda"):
+    tp = (rank, world, group): tensor-parallel over `world` GPUs with `weights` already sharded by shard_weights;
+    the out-projection and down-projection write fp32 partial sums that one NCCL all-reduce each per block adds up
+    (two per block, the block being two sequential sublayers), and the residual / LayerNorm run replicated."""
+
+    def __init__(self, cfg, weights, device="cuda", tp=None):
         self.cfg = cfg
         dev = torch.device(device)
         self.dev = dev
-        D, F, M, H = cfg.hidden, cfg.ffn, cfg.M, cfg.heads
+        self.tp = tp
+        world = tp[1] if tp else 1
+        D, M = cfg.hidden, cfg.M
+        H, F = cfg.heads // world, cfg.ffn // world
+        self.heads_local = H
         pw = ops.PackedWeight.from_float
         self.blocks = []
         for b in weights["blocks"]:
@@ -111,13 +141,14 @@ class DiT:
         self.x = [torch.empty(M, D, **bf) for _ in range(2)]
         self.emb = torch.empty(M, D, **bf)
         self.a = torch.empty(M, D, **bf)
-        self.qkv = torch.empty(M, 3 * D, **bf)
+        self.qkv = torch.empty(M, 3 * H * HEAD_DIM, **bf)
         self.ldv = (M + 127) // 128 * 128
         self.q = torch.empty(H, M, 128, **bf)
         self.k = torch.empty(H, M, 128, **bf)
         self.vt = torch.empty(H, 128, self.ldv, **bf)
-        self.o = torch.empty(M, D, **bf)
+        self.o = torch.empty(M, H * HEAD_DIM, **bf)
         self.c = torch.empty(M, D, **bf)
+        self.c32 = torch.empty(M, D, dtype=torch.float32, device=dev) if tp else None
         self.h = torch.empty(M, F, **bf)
         self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
         self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
@@ -144,7 +175,8 @@ class DiT:
 
     def _ln(self, x, br, params, xo, y):
         M, D = x.shape
-        L.call("rl_ln_mod", x.data_ptr(), None if br is None else br.data_ptr(), params.data_ptr(), M, D,
+        bdt = L.RL_F32 if (br is not None and br.dtype == torch.float32) else L.RL_BF16
+        L.call("rl_ln_mod", x.data_ptr(), None if br is None else br.data_ptr(), bdt, params.data_ptr(), M, D,
                self.cfg.text, None if xo is None else xo.data_ptr(), y.data_ptr(), None,
                torch.cuda.current_stream().cuda_stream)
 
@@ -159,20 +191,30 @@ class DiT:
         self.emb[:cfg.text].copy_(text_states.to(self.dev, torch.bfloat16))
         self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
 
+    def _branch(self, x, w):
+        """The out / down projection: bf16 on one GPU; fp32 partial sums all-reduced across the TP group."""
+        if not self.tp:
+            self._linear(x, w, self.c)
+            return self.c
+        self._linear(x, w, self.c32, out_dtype=L.RL_F32)
+        import torch.distributed as dist
+        dist.all_reduce(self.c32, group=self.tp[2])
+        return self.c32
+
     def block(self, i, last=False):
         cfg, b = self.cfg, self.blocks[i]
         s = torch.cuda.current_stream().cuda_stream
-        M, H = cfg.M, cfg.heads
+        M, H = cfg.M, self.heads_local
         self._linear(self.a, b["qkv"], self.qkv)
         L.call("rl_qkv_post", self.qkv.data_ptr(), self.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(),
                M, H, self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
         L.call("rl_attention", self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, H, M, M, M, None,
-               1.0, self.o.data_ptr(), cfg.hidden, s)
-        self._linear(self.o, b["o"], self.c)
-        self._ln(self.x[0], self.c, self.params["mlp"], self.x[1], self.a)
+               1.0, self.o.data_ptr(), H * HEAD_DIM, s)
+        c = self._branch(self.o, b["o"])
+        self._ln(self.x[0], c, self.params["mlp"], self.x[1], self.a)
         self._linear(self.a, b["up"], self.h, epi=L.RL_EPI_SWIGLU)
-        self._linear(self.h, b["down"], self.c)
-        self._ln(self.x[1], self.c, self.params["out" if last else "attn"], self.x[0], self.a)
+        c = self._branch(self.h, b["down"])
+        self._ln(self.x[1], c, self.params["out" if last else "attn"], self.x[0], self.a)
 
     def project(self):
         """proj_out on the image rows of a (= norm_out output) -> velocity (image, 64) float32 (forward.py:261-269)."""

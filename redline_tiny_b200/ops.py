@@ -163,7 +163,8 @@ def ln_mod(x, branch, params, row_split=0, want_x=True, want_y_bytes=False):
     xo = torch.empty_like(x) if want_x else None
     y = torch.empty_like(x)
     yq = torch.empty(M * D // 8 * 9, dtype=torch.uint8, device=x.device) if want_y_bytes else None
-    L.call("rl_ln_mod", _ptr(x), _ptr(branch), _ptr(params), M, D, int(row_split), _ptr(xo), _ptr(y), _ptr(yq),
+    bdt = L.RL_BF16 if branch is None else _dtype_code(branch)
+    L.call("rl_ln_mod", _ptr(x), _ptr(branch), bdt, _ptr(params), M, D, int(row_split), _ptr(xo), _ptr(y), _ptr(yq),
            _stream())
     return xo, y, yq
 
