@@ -40,9 +40,11 @@ typedef enum {
 
 typedef enum { RL_F32 = 0, RL_BF16 = 1 } rl_dtype;
 
-/* Stream order of bfp16 blocks. RL_ROWMAJOR: block (r, c/8) of an (M, K) matrix at index r*K/8 + c/8.
- * RL_A_LAYOUT: the reference's GEMM A-operand order, a_layout(A, 128, 64) (npu_layouts.py:18-23). */
-typedef enum { RL_ROWMAJOR = 0, RL_A_LAYOUT = 1 } rl_layout;
+/* Stream order of 8-value blocks of an (M, K) matrix. RL_ROWMAJOR: block (r, c/8) at index r*K/8 + c/8.
+ * RL_A_LAYOUT: the reference's GEMM A-operand order, a_layout(A, 128, 64) (npu_layouts.py:18-23; M % 128, K % 64).
+ * RL_C_ATB: the order its GEMMs emit C and keep the residual stream in, c_layout_atb(C, 128, 128)
+ * (npu_layouts.py:31-48; M % 512, K % 1024). */
+typedef enum { RL_ROWMAJOR = 0, RL_A_LAYOUT = 1, RL_C_ATB = 2 } rl_layout;
 
 typedef enum {
   RL_EPI_NONE = 0,   /* C = A @ B */
@@ -77,6 +79,13 @@ int rl_quantize_bfp16(const void* x, int x_dtype, int64_t M, int64_t K, int layo
  */
 int rl_dequantize_bfp16(const uint8_t* q, int layout, int64_t M, int64_t K, void* out, int out_dtype,
                         rl_stream_t stream);
+
+/*
+ * a3/a5 - bf16 (M, K) between stream orders (row-major, a_layout, the ATB C order): the reference keeps its bf16
+ * residual stream in the C order (run_ln.ln_pack_x, redline/run_ln.py:28-30; c_unlayout_atb for reading it back).
+ */
+int rl_permute_bf16(const uint16_t* src, int src_layout, uint16_t* dst, int dst_layout, int64_t M, int64_t K,
+                    rl_stream_t stream);
 
 /*
  * a4/a6 - the reference's packed-weight stream on the GPU. Replaces pack_weights.pack_b

@@ -12,7 +12,7 @@ LIB_PATH = os.path.join(HERE, "libredline_b200.so")
 
 RL_OK, RL_ERR_ARGUMENT, RL_ERR_ALIGNMENT, RL_ERR_UNSUPPORTED, RL_ERR_CUDA, RL_ERR_DEVICE = 0, -1, -2, -3, -4, -5
 RL_F32, RL_BF16 = 0, 1
-RL_ROWMAJOR, RL_A_LAYOUT = 0, 1
+RL_ROWMAJOR, RL_A_LAYOUT, RL_C_ATB = 0, 1, 2
 RL_EPI_NONE, RL_EPI_BIAS, RL_EPI_SWIGLU = 0, 1, 2
 
 _P = ctypes.c_void_p
@@ -27,6 +27,7 @@ SIGNATURES = {
     "rl_quantize_bfp16": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _P]),
     "rl_dequantize_bfp16": (_I, [_P, _I, _I64, _I64, _P, _I, _P]),
     "rl_pack_b": (_I, [_P, _I, _I64, _I64, _P, _P]),
+    "rl_permute_bf16": (_I, [_P, _I, _P, _I, _I64, _I64, _P]),
     "rl_weights_from_pack_b": (_I, [_P, _I64, _I64, _I, _P, _P]),
     "rl_pack_weights": (_I, [_P, _I, _I64, _I64, _I, _P, _P]),
     "rl_linear_bfp16": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P]),

@@ -13,12 +13,16 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kStageBytes = 32 * 9;  // one warp's blocks
 
 // Source coordinates (row, first column) of output block `ob` of an (M, K) matrix in the given stream order.
+//   RL_ROWMAJOR : block (r, c/8) at r*K/8 + c/8;
+//   RL_A_LAYOUT : a_layout(., 128, 64) (npu_layouts.py:18-23): 1024 blocks per tile; inside (sbr, bc, bis, rib);
+//   RL_C_ATB    : c_layout_atb(., 128, 128) (npu_layouts.py:31-48): groups of 4 x 8 tiles of 128 x 128, per group
+//                 one chunk per core column stacking its 4 row tiles; inside 2x2 super-blocks of row-major 8x8.
 __device__ __forceinline__ void block_coords(int layout, int64_t ob, int64_t K, int64_t& r, int64_t& c0) {
   if (layout == RL_ROWMAJOR) {
     const int64_t kb = K >> 3;
     r = ob / kb;
     c0 = (ob - r * kb) << 3;
-  } else {  // a_layout(., 128, 64): 1024 blocks per tile; inside: (sbr, bc, bis, rib)
+  } else if (layout == RL_A_LAYOUT) {
     const int64_t tile = ob >> 10;
     const int w = static_cast<int>(ob & 1023);
     const int64_t kt_n = K >> 6;
@@ -26,7 +30,42 @@ __device__ __forceinline__ void block_coords(int layout, int64_t ob, int64_t K, 
     const int sbr = w >> 7, bc = (w >> 4) & 7, bis = (w >> 3) & 1, rib = w & 7;
     r = tr * 128 + sbr * 16 + bis * 8 + rib;
     c0 = tc * 64 + bc * 8;
+  } else {  // RL_C_ATB: ob = ((((((rg*CG + cg)*8 + col)*4 + row)*8 + sbr)*8 + sbc)*2 + br)*2 + bc)*8 + rib
+    int64_t t = ob;
+    const int rib = static_cast<int>(t & 7); t >>= 3;
+    const int bc = static_cast<int>(t & 1); t >>= 1;
+    const int br = static_cast<int>(t & 1); t >>= 1;
+    const int sbc = static_cast<int>(t & 7); t >>= 3;
+    const int sbr = static_cast<int>(t & 7); t >>= 3;
+    const int row = static_cast<int>(t & 3); t >>= 2;
+    const int col = static_cast<int>(t & 7); t >>= 3;
+    const int64_t cgn = K >> 10;
+    const int64_t rg = t / cgn, cg = t - rg * cgn;
+    r = rg * 512 + row * 128 + sbr * 16 + br * 8 + rib;
+    c0 = cg * 1024 + col * 128 + sbc * 16 + bc * 8;
   }
+}
+
+// Inverse of block_coords: the stream block index of the 8 values (r, c0 .. c0+7).
+__device__ __forceinline__ int64_t block_index(int layout, int64_t r, int64_t c0, int64_t K) {
+  if (layout == RL_ROWMAJOR) return r * (K >> 3) + (c0 >> 3);
+  if (layout == RL_A_LAYOUT) {
+    const int64_t tile = (r >> 7) * (K >> 6) + (c0 >> 6);
+    const int64_t w = ((((r & 127) >> 4) * 8 + ((c0 & 63) >> 3)) * 2 + ((r >> 3) & 1)) * 8 + (r & 7);
+    return tile * 1024 + w;
+  }
+  const int64_t rg = r >> 9, row = (r >> 7) & 3, sbr = (r >> 4) & 7, br = (r >> 3) & 1, rib = r & 7;
+  const int64_t cg = c0 >> 10, col = (c0 >> 7) & 7, sbc = (c0 >> 4) & 7, bc = (c0 >> 3) & 1;
+  int64_t i = (rg * (K >> 10) + cg) * 8 + col;
+  i = ((((i * 4 + row) * 8 + sbr) * 8 + sbc) * 2 + br) * 2 + bc;
+  return i * 8 + rib;
+}
+
+inline bool layout_ok(int layout, int64_t M, int64_t K) {
+  if (layout == RL_ROWMAJOR) return K % 8 == 0;
+  if (layout == RL_A_LAYOUT) return M % 128 == 0 && K % 64 == 0;
+  if (layout == RL_C_ATB) return M % 512 == 0 && K % 1024 == 0;
+  return false;
 }
 
 template <typename T>
@@ -135,6 +174,19 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const T* __restrict_
       if (q) stage_put(stage[warp], lane, E, lo, hi);
     }
     if (q) stage_flush(stage[warp], q, base, nblocks, lane);
+  }
+}
+
+// bf16 (M, K) in one stream order -> another; the orders keep 8 consecutive columns together, so 16-byte moves.
+__global__ void __launch_bounds__(kThreads) permute_bf16_kernel(const uint16_t* __restrict__ src, int src_layout,
+                                                                uint16_t* __restrict__ dst, int dst_layout, int64_t K,
+                                                                int64_t nblocks) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t ob = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; ob < nblocks; ob += stride) {
+    int64_t r, c0;
+    block_coords(dst_layout, ob, K, r, c0);
+    const int64_t ib = block_index(src_layout, r, c0, K);
+    reinterpret_cast<uint4*>(dst)[ob] = __ldg(reinterpret_cast<const uint4*>(src) + ib);
   }
 }
 
@@ -285,10 +337,11 @@ int rl_quantize_bfp16(const void* x, int x_dtype, int64_t M, int64_t K, int layo
   RL_REQUIRE(M >= 0 && K > 0 && K % 8 == 0, RL_ERR_ARGUMENT, "rl_quantize_bfp16: need K %% 8 == 0 (M=%lld K=%lld)",
              (long long)M, (long long)K);
   RL_REQUIRE(x_dtype == RL_F32 || x_dtype == RL_BF16, RL_ERR_ARGUMENT, "rl_quantize_bfp16: bad dtype %d", x_dtype);
-  RL_REQUIRE(layout == RL_ROWMAJOR || layout == RL_A_LAYOUT, RL_ERR_ARGUMENT, "rl_quantize_bfp16: bad layout %d",
+  RL_REQUIRE(layout == RL_ROWMAJOR || layout == RL_A_LAYOUT || layout == RL_C_ATB, RL_ERR_ARGUMENT,
+             "rl_quantize_bfp16: bad layout %d", layout);
+  RL_REQUIRE(codec::layout_ok(layout, M, K), RL_ERR_ARGUMENT,
+             "rl_quantize_bfp16: layout %d needs M %% 128 and K %% 64 (a_layout) or M %% 512 and K %% 1024 (C order)",
              layout);
-  RL_REQUIRE(layout == RL_ROWMAJOR || (M % 128 == 0 && K % 64 == 0), RL_ERR_ARGUMENT,
-             "rl_quantize_bfp16: a_layout needs M %% 128 == 0 and K %% 64 == 0");
   RL_REQUIRE(aligned(x, 16) && aligned(q_out, 16) && aligned(dq_out, 16), RL_ERR_ALIGNMENT,
              "rl_quantize_bfp16: pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_quantize_bfp16: needs an sm_100 device");
@@ -310,8 +363,9 @@ int rl_dequantize_bfp16(const uint8_t* q, int layout, int64_t M, int64_t K, void
   RL_REQUIRE(q != nullptr && out != nullptr, RL_ERR_ARGUMENT, "rl_dequantize_bfp16: NULL pointer");
   RL_REQUIRE(M >= 0 && K > 0 && K % 8 == 0, RL_ERR_ARGUMENT, "rl_dequantize_bfp16: need K %% 8 == 0");
   RL_REQUIRE(out_dtype == RL_F32 || out_dtype == RL_BF16, RL_ERR_ARGUMENT, "rl_dequantize_bfp16: bad dtype");
-  RL_REQUIRE(layout == RL_ROWMAJOR || (layout == RL_A_LAYOUT && M % 128 == 0 && K % 64 == 0), RL_ERR_ARGUMENT,
-             "rl_dequantize_bfp16: bad layout / shape");
+  RL_REQUIRE((layout == RL_ROWMAJOR || layout == RL_A_LAYOUT || layout == RL_C_ATB) &&
+                 codec::layout_ok(layout, M, K),
+             RL_ERR_ARGUMENT, "rl_dequantize_bfp16: bad layout / shape");
   RL_REQUIRE(aligned(q, 16) && aligned(out, 16), RL_ERR_ALIGNMENT, "rl_dequantize_bfp16: pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_dequantize_bfp16: needs an sm_100 device");
   const int64_t nblocks = M * K / 8;
@@ -323,6 +377,22 @@ int rl_dequantize_bfp16(const uint8_t* q, int layout, int64_t M, int64_t K, void
   else
     codec::dequantize_kernel<uint16_t><<<grid, codec::kThreads, 0, stream>>>(q, K, layout,
                                                                              static_cast<uint16_t*>(out), nblocks);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+int rl_permute_bf16(const uint16_t* src, int src_layout, uint16_t* dst, int dst_layout, int64_t M, int64_t K,
+                    rl_stream_t stream) {
+  RL_REQUIRE(src && dst && src != dst, RL_ERR_ARGUMENT, "rl_permute_bf16: NULL or aliased pointers");
+  RL_REQUIRE(src_layout >= RL_ROWMAJOR && src_layout <= RL_C_ATB && dst_layout >= RL_ROWMAJOR &&
+                 dst_layout <= RL_C_ATB && codec::layout_ok(src_layout, M, K) && codec::layout_ok(dst_layout, M, K),
+             RL_ERR_ARGUMENT, "rl_permute_bf16: bad layout / shape");
+  RL_REQUIRE(aligned(src, 16) && aligned(dst, 16), RL_ERR_ALIGNMENT, "rl_permute_bf16: pointers must be 16-byte aligned");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_permute_bf16: needs an sm_100 device");
+  const int64_t nblocks = M * K / 8;
+  if (nblocks == 0) return RL_OK;
+  codec::permute_bf16_kernel<<<codec::grid_for(nblocks), codec::kThreads, 0, stream>>>(src, src_layout, dst,
+                                                                                         dst_layout, K, nblocks);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

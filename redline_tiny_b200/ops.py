@@ -45,7 +45,16 @@ def _dtype_code(t):
     raise ValueError(f"unsupported dtype {t.dtype}")
 
 
-_LAYOUTS = {"rowmajor": L.RL_ROWMAJOR, "a_layout": L.RL_A_LAYOUT}
+_LAYOUTS = {"rowmajor": L.RL_ROWMAJOR, "a_layout": L.RL_A_LAYOUT, "c_atb": L.RL_C_ATB}
+
+
+def permute_bf16(x, M, K, src="rowmajor", dst="c_atb", out=None):
+    """bf16 (M, K) values from one stream order to another (flat tensors for the NPU orders)."""
+    _check_cuda(x, out)
+    if out is None:
+        out = torch.empty(M * K, dtype=torch.bfloat16, device=x.device)
+    L.call("rl_permute_bf16", _ptr(x), _LAYOUTS[src], _ptr(out), _LAYOUTS[dst], M, K, _stream())
+    return out
 
 
 def quantize_bfp16(x, layout="rowmajor", want_bytes=True, want_decoded=True):
