@@ -132,64 +132,75 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
   }
 }
 
-// One warp per (token, head) of Q or K: lane l owns dims 4l..4l+3 (two RoPE pairs).
-// qkv: (M, 3 * H * 128) bf16 = [q heads | k heads | v heads]; cs: (M, 64, 2) float32 (cos, sin) per token and pair;
-// wq, wk: float32 [128]. Out: q, k as (H, M, 128) bf16.
-__global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const uint16_t* __restrict__ qkv,
-                                                                const float* __restrict__ cs,
-                                                                const float* __restrict__ wq,
-                                                                const float* __restrict__ wk, int64_t M, int H,
-                                                                float eps, uint16_t* __restrict__ q,
-                                                                uint16_t* __restrict__ k) {
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+// One warp per token: lane l owns dims 4l..4l+3 (two RoPE pairs) of every q and k head; the token's (cos, sin) and
+// the norm weights are loaded once.
+__global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16_t* __restrict__ qkv,
+                                                                    const float* __restrict__ cs,
+                                                                    const float* __restrict__ wq,
+                                                                    const float* __restrict__ wk, int64_t M, int H,
+                                                                    float eps, uint16_t* __restrict__ q,
+                                                                    uint16_t* __restrict__ k) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t units = M * H * 2;   // (token, head, q|k)
   const int64_t ld = static_cast<int64_t>(3) * H * 128;
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * kWarps + warp; u < units;
-       u += static_cast<int64_t>(gridDim.x) * kWarps) {
-    const int which = static_cast<int>(u & 1);          // 0 = q, 1 = k
-    const int64_t th = u >> 1;
-    const int64_t m = th / H;
-    const int h = static_cast<int>(th - m * H);
-    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(qkv + m * ld + (static_cast<int64_t>(which) * H + h) * 128) + lane);
-    float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u), __uint_as_float(raw.y << 16),
-                  __uint_as_float(raw.y & 0xFFFF0000u)};
-    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
-    const float4 w = __ldg(reinterpret_cast<const float4*>(which ? wk : wq) + lane);
-    const float n0 = v[0] * inv * w.x, n1 = v[1] * inv * w.y, n2 = v[2] * inv * w.z, n3 = v[3] * inv * w.w;
+  const float4 w_q = __ldg(reinterpret_cast<const float4*>(wq) + lane);
+  const float4 w_k = __ldg(reinterpret_cast<const float4*>(wk) + lane);
+  for (int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + warp; m < M; m += static_cast<int64_t>(gridDim.x) * kWarps) {
     const float4 c = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + lane);  // (cos, sin) of pairs 2l, 2l+1
-    const float o0 = n0 * c.x - n1 * c.y, o1 = n0 * c.y + n1 * c.x;
-    const float o2 = n2 * c.z - n3 * c.w, o3 = n2 * c.w + n3 * c.z;
-    uint16_t* dst = (which ? k : q) + (static_cast<int64_t>(h) * M + m) * 128;
-    reinterpret_cast<uint2*>(dst)[lane] = make_uint2(float_to_bf16_bits(o0) | (float_to_bf16_bits(o1) << 16),
-                                                     float_to_bf16_bits(o2) | (float_to_bf16_bits(o3) << 16));
+    const uint16_t* row = qkv + m * ld;
+#pragma unroll 2
+    for (int u = 0; u < 2 * H; ++u) {                 // u < H: q head u; else k head u - H
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(row + static_cast<int64_t>(u) * 128) + lane);
+      const float v0 = __uint_as_float(raw.x << 16), v1 = __uint_as_float(raw.x & 0xFFFF0000u);
+      const float v2 = __uint_as_float(raw.y << 16), v3 = __uint_as_float(raw.y & 0xFFFF0000u);
+      const float ss = warp_sum(v0 * v0 + v1 * v1 + v2 * v2 + v3 * v3);
+      const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
+      const float4 w = u < H ? w_q : w_k;
+      const float n0 = v0 * inv * w.x, n1 = v1 * inv * w.y, n2 = v2 * inv * w.z, n3 = v3 * inv * w.w;
+      const float o0 = n0 * c.x - n1 * c.y, o1 = n0 * c.y + n1 * c.x;
+      const float o2 = n2 * c.z - n3 * c.w, o3 = n2 * c.w + n3 * c.z;
+      uint16_t* dst = (u < H ? q + (static_cast<int64_t>(u) * M + m) * 128 : k + (static_cast<int64_t>(u - H) * M + m) * 128);
+      reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack_bf16x2_rn(o0, o1), pack_bf16x2_rn(o2, o3));
+    }
   }
 }
 
-// V (the third third of qkv) -> vt (H, 128, ldv): 64 tokens x 128 dims per CTA through shared memory.
-__global__ void __launch_bounds__(kThreads) v_transpose_kernel(const uint16_t* __restrict__ qkv, int64_t M, int H,
-                                                               int64_t ldv, uint16_t* __restrict__ vt) {
-  __shared__ uint16_t tile[64][128 + 2];
+// V (the third third of qkv) -> vt (H, 128, ldv): 64 tokens x 128 dims per CTA, 16-byte loads and stores through a
+// padded shared tile [dim][token].
+__global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t* __restrict__ qkv, int64_t M, int H,
+                                                                 int64_t ldv, uint16_t* __restrict__ vt) {
+  __shared__ __align__(16) uint16_t tile[128][64 + 8];
   const int64_t ld = static_cast<int64_t>(3) * H * 128;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64;
   const int h = blockIdx.y;
-  for (int i = threadIdx.x; i < 64 * 64; i += kThreads) {  // 64 tokens x 64 bf16 pairs
-    const int t = i >> 6, d2 = i & 63;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {                    // 64 tokens x 16 chunks of 8 dims
+    const int cid = threadIdx.x + it * kThreads;
+    const int t = cid >> 4, dg = cid & 15;
     const int64_t m = m0 + t;
-    uint32_t w = 0;
-    if (m < M) w = __ldg(reinterpret_cast<const uint32_t*>(qkv + m * ld + (static_cast<int64_t>(2) * H + h) * 128) + d2);
-    tile[t][2 * d2] = static_cast<uint16_t>(w);
-    tile[t][2 * d2 + 1] = static_cast<uint16_t>(w >> 16);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (m < M) v = __ldg(reinterpret_cast<const uint4*>(qkv + m * ld + (static_cast<int64_t>(2) * H + h) * 128) + dg);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tile[8 * dg + 2 * i][t] = static_cast<uint16_t>(wv[i]);
+      tile[8 * dg + 2 * i + 1][t] = static_cast<uint16_t>(wv[i] >> 16);
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 128 * 32; i += kThreads) {  // 128 dims x 32 token pairs
-    const int d = i >> 5, t2 = i & 31;
-    const int64_t m = m0 + 2 * t2;
-    if (m < ldv) {
-      const uint32_t w = static_cast<uint32_t>(tile[2 * t2][d]) | (static_cast<uint32_t>(tile[2 * t2 + 1][d]) << 16);
-      *reinterpret_cast<uint32_t*>(vt + (static_cast<int64_t>(h) * 128 + d) * ldv + m) = w;
-    }
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {                    // 128 dims x 8 chunks of 8 tokens
+    const int cid = threadIdx.x + it * kThreads;
+    const int d = cid >> 3, tc = cid & 7;
+    const int64_t m = m0 + 8 * tc;
+    if (m < ldv)
+      *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(h) * 128 + d) * ldv + m) =
+          *reinterpret_cast<const uint4*>(&tile[d][8 * tc]);
   }
 }
 
@@ -231,11 +242,11 @@ int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, con
              RL_ERR_ALIGNMENT, "rl_qkv_post: pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_qkv_post: needs an sm_100 device");
   if (M == 0) return RL_OK;
-  glue::qk_norm_rope_kernel<<<glue::grid_rows(M * H * 2, glue::kWarps), glue::kThreads, 0, stream>>>(
+  glue::qk_norm_rope_tok_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
       qkv, rope_cs, w_q, w_k, M, H, 1e-6f, q, k);
   RL_TRY_CUDA(cudaGetLastError());
   const dim3 grid(static_cast<unsigned>((ldv + 63) / 64), static_cast<unsigned>(H));
-  glue::v_transpose_kernel<<<grid, glue::kThreads, 0, stream>>>(qkv, M, H, ldv, vt);
+  glue::v_transpose16_kernel<<<grid, glue::kThreads, 0, stream>>>(qkv, M, H, ldv, vt);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }
