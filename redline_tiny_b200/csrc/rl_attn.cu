@@ -12,9 +12,12 @@
 //   softmax              4 warps, thread = query row = TMEM lane: tcgen05.ld of the row, mask, max, exp2, row sum;
 //                        P (bf16) written back over the same TMEM columns with tcgen05.st;
 //   O += P_j V_j         tcgen05.mma with A = P from TMEM, B = V^T (dims x keys, keys contiguous) in shared memory.
-// Warp roles: warp 0 = TMA producer + TMEM allocator, warp 1 = MMA issuer, warps 4-7 = softmax / correction /
-// epilogue. O / l is rounded to bfp16 blocks of 8 along the head dim (the out-projection's A operand) and written
-// row-major at columns h*128.. of the output.
+// K and V tiles have separate three-stage pipelines: a K stage is released as soon as its QK product completes, so
+// the producer keeps K loads about two blocks ahead of use (with one shared stage per block the load of block j+2
+// could only start after P.V of block j-1, and it arrived late).
+// Warp roles: warp 0 = TMA producer + TMEM allocator, warp 1 = MMA issuer (warp-wide loop, elected lane issues),
+// warps 2-5 = softmax / correction / epilogue. O / l is rounded to bfp16 blocks of 8 along the head dim (the out-projection's A
+// operand) and written row-major at columns h*128.. of the output.
 #include "rl_common.cuh"
 #include "rl_host.h"
 
@@ -22,28 +25,32 @@ namespace rl {
 namespace attn {
 
 constexpr int BQ = 128;                  // queries per CTA (TMEM lanes)
-constexpr int BKV = 128;                 // keys per block
 constexpr int HD = 128;                  // head dim
-constexpr int HALF_BYTES = 128 * 64 * 2; // one 128-row x 64-element SW128 sub-tile (16 KB)
-constexpr int TILE_BYTES = 2 * HALF_BYTES;
-constexpr int kStages = 3;               // K/V stages
-constexpr int kThreads = 256;
+constexpr int BKV = 128;                 // keys per block
+constexpr int SUB_ROWS_BYTES = 128;      // one swizzle row: 64 bf16
+constexpr int kThreads = 192;            // producer, MMA issuer, 4 softmax warps
 constexpr float kTau = 8.0f;             // lazy-rescale threshold (log2 units)
-
-struct Smem {
-  // 1024-aligned tiles: Q, then per stage K and V^T
-  static constexpr int kQ = 0;
-  static constexpr int kK = TILE_BYTES;
-  static constexpr int kV = kK + kStages * TILE_BYTES;
-  static constexpr int kBar = kV + kStages * TILE_BYTES;
-  static constexpr int kBytes = 1024 + kBar + 256;
-};
-static_assert(Smem::kBytes <= 232448, "shared memory");
+constexpr int kStages = 3;               // depth of each of the K and V pipelines
+constexpr int Q_BYTES = BQ * HD * 2;     // two 128 x 64 sub-tiles
+constexpr int K_SUB = BKV * SUB_ROWS_BYTES;
+constexpr int K_BYTES = 2 * K_SUB;
+constexpr int V_SUB = HD * SUB_ROWS_BYTES;   // 128 dims x 64 keys
+constexpr int V_BYTES = (BKV / 64) * V_SUB;
+constexpr int kQ = 0;
+constexpr int kK = Q_BYTES;
+constexpr int kV = kK + kStages * K_BYTES;
+constexpr int kBar = kV + kStages * V_BYTES;
+constexpr int kBytes = 1024 + kBar + 256;
+constexpr int kTmemCols = 512;               // S buffers (2 x 128) + O (128), rounded to a power of two
+constexpr int kOCol = 2 * BKV;
+static_assert(kBytes <= 232448, "shared memory");
 
 struct Barriers {
   uint64_t q_full;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t pv_done[2];
@@ -52,12 +59,13 @@ struct Barriers {
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 struct Params {
   int64_t Nq, Nk, nkv;
   int H;
   const int32_t* row_limit;   // per query row: last visible key (inclusive), or null
-  float scale_log2;           // logits = (q . k) * scale_log2, in log2 units
+  float scale_log2;           // logits = (q . k) * scale_log2, in log2 units (> 0)
   uint16_t* o;
   int64_t ldo;
   int nblk;
@@ -68,6 +76,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Two floats -> bf16x2 (round to nearest even), low half = a.
@@ -85,12 +100,26 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Bookkeeping of one load pipeline for the producer's error path: which stages have a load in flight, and the
+// parity of its phase.
+struct InFlight {
+  uint32_t issued = 0, parity = 0;
+  __device__ void note(int s, uint32_t ph) {
+    issued |= 1u << s;
+    parity = (parity & ~(1u << s)) | (ph << s);
+  }
+  __device__ void drain(uint64_t* full) const {
+    for (int s = 0; s < kStages; ++s)
+      if (issued & (1u << s)) mbar_drain(&full[s], (parity >> s) & 1);
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + Smem::kBar);
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kBar);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y;
@@ -99,8 +128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->s_full[b], 1);
@@ -116,90 +147,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_v);
   }
   if (warp == 0) {
-    tmem_alloc(&bars->tmem_base, 512);
+    tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = bars->tmem_base;   // S buffers: columns [0,128), [128,256); O: [256, 384)
-  const uint32_t t_o = tmem + 256;
+  const uint32_t tmem = bars->tmem_base;   // S buffers: columns [0, 128), [128, 256); O: [256, 384)
+  const uint32_t t_o = tmem + kOCol;
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- producer: Q, then K(t) and V(t - 1) in turn (K one block ahead of V) ----------------
     if (lane == 0) {
       bool ok = true;
-      uint32_t issued = 0, last_par = 0;
-      mbar_arrive_expect_tx(&bars->q_full, TILE_BYTES);
-      tma_load_3d(smem + Smem::kQ, &tm_q, &bars->q_full, 0, qt * BQ, h);
-      tma_load_3d(smem + Smem::kQ + HALF_BYTES, &tm_q, &bars->q_full, 64, qt * BQ, h);
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&bars->kv_empty[s], ph ^ 1, abort)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bars->kv_full[s], 2 * TILE_BYTES);
-        uint8_t* kt = smem + Smem::kK + s * TILE_BYTES;
-        uint8_t* vt = smem + Smem::kV + s * TILE_BYTES;
-        tma_load_3d(kt, &tm_k, &bars->kv_full[s], 0, j * BKV, h);
-        tma_load_3d(kt + HALF_BYTES, &tm_k, &bars->kv_full[s], 64, j * BKV, h);
-        tma_load_3d(vt, &tm_v, &bars->kv_full[s], j * BKV, 0, h);
-        tma_load_3d(vt + HALF_BYTES, &tm_v, &bars->kv_full[s], j * BKV + 64, 0, h);
-        issued |= 1u << s;
-        last_par = (last_par & ~(1u << s)) | (ph << s);
+      InFlight kf, vf;
+      mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
+      tma_load_3d(smem + kQ, &tm_q, &bars->q_full, 0, qt * BQ, h);
+      tma_load_3d(smem + kQ + Q_BYTES / 2, &tm_q, &bars->q_full, 64, qt * BQ, h);
+      for (int t = 0; ok && t <= nblk; ++t) {
+        if (t < nblk) {
+          const int s = t % kStages;
+          const uint32_t ph = (t / kStages) & 1;
+          if (!mbar_wait(&bars->k_empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->k_full[s], K_BYTES);
+          uint8_t* kt = smem + kK + s * K_BYTES;
+          tma_load_3d(kt, &tm_k, &bars->k_full[s], 0, t * BKV, h);
+          tma_load_3d(kt + K_SUB, &tm_k, &bars->k_full[s], 64, t * BKV, h);
+          kf.note(s, ph);
+        }
+        if (t >= 1) {
+          const int j = t - 1, s = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          if (!mbar_wait(&bars->v_empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->v_full[s], V_BYTES);
+          uint8_t* vt = smem + kV + s * V_BYTES;
+          tma_load_3d(vt, &tm_v, &bars->v_full[s], j * BKV, 0, h);
+          tma_load_3d(vt + V_SUB, &tm_v, &bars->v_full[s], j * BKV + 64, 0, h);
+          vf.note(s, ph);
+        }
       }
       if (!ok) {
         mbar_drain(&bars->q_full, 0);
-        for (int s = 0; s < kStages; ++s)
-          if (issued & (1u << s)) mbar_drain(&bars->kv_full[s], (last_par >> s) & 1);
+        kf.drain(bars->k_full);
+        vf.drain(bars->v_full);
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BQ, BKV);
-      bool ok = true, any = false;
-      const uint32_t qa = smem_u32(smem + Smem::kQ);
-      auto issue_pv = [&](int jj) -> bool {
-        const int sb = jj & 1, s = jj % kStages;
-        if (!mbar_wait(&bars->p_full[sb], (jj >> 1) & 1, abort)) return false;
-        tc_fence_after();
-        const uint32_t vb = smem_u32(smem + Smem::kV + s * TILE_BYTES);
+    // ---------------- MMA issuer: the whole warp runs the loop, one elected lane issues ----------------
+    constexpr uint32_t idesc_s = idesc_bf16(BQ, BKV);   // S = Q K^T: M 128 (queries) x N 128 (keys)
+    constexpr uint32_t idesc_o = idesc_bf16(BQ, HD);    // O += P V: M 128 (queries) x N 128 (dims)
+    bool ok = true, any = false;
+    const uint32_t qa = smem_u32(smem + kQ);
+    auto issue_pv = [&](int jj) -> bool {
+      const int sb = jj & 1, s = jj % kStages;
+      if (!mbar_wait_warp(&bars->v_full[s], (jj / kStages) & 1, abort)) return false;
+      if (!mbar_wait_warp(&bars->p_full[sb], (jj >> 1) & 1, abort)) return false;
+      tc_fence_after();
+      const uint32_t vb = smem_u32(smem + kV + s * V_BYTES);
+      if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k) {
-          const uint64_t bdesc = sdesc_kmajor_sw128(vb + (k >> 2) * HALF_BYTES) + 2 * (k & 3);
-          umma_ts(t_o, tmem + sb * 128 + k * 8, bdesc, idesc, (jj | k) ? 1u : 0u);
+          const uint64_t bdesc = sdesc_kmajor_sw128(vb + (k >> 2) * V_SUB) + 2 * (k & 3);
+          umma_ts(t_o, tmem + sb * BKV + k * 8, bdesc, idesc_o, (jj | k) ? 1u : 0u);
         }
-        umma_commit(&bars->kv_empty[s]);
+        umma_commit(&bars->v_empty[s]);
         umma_commit(&bars->pv_done[sb]);
-        return true;
-      };
-      if (!mbar_wait(&bars->q_full, 0, abort)) ok = false;
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j % kStages, sb = j & 1;
-        if (!mbar_wait(&bars->kv_full[s], (j / kStages) & 1, abort)) { ok = false; break; }
-        // S buffer sb is free once PV of block j - 2 (which read P from it) has completed
-        if (!mbar_wait(&bars->pv_done[sb], ((j >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t kb = smem_u32(smem + Smem::kK + s * TILE_BYTES);
+      }
+      __syncwarp();
+      return true;
+    };
+    if (!mbar_wait_warp(&bars->q_full, 0, abort)) ok = false;
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int s = j % kStages, sb = j & 1;
+      if (!mbar_wait_warp(&bars->k_full[s], (j / kStages) & 1, abort)) { ok = false; break; }
+      // S buffer sb is free once P.V of block j - 2 (which read P from it) has completed
+      if (!mbar_wait_warp(&bars->pv_done[sb], ((j >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t kb = smem_u32(smem + kK + s * K_BYTES);
+      if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
-          const uint64_t adesc = sdesc_kmajor_sw128(qa + (k >> 2) * HALF_BYTES) + 2 * (k & 3);
-          const uint64_t bdesc = sdesc_kmajor_sw128(kb + (k >> 2) * HALF_BYTES) + 2 * (k & 3);
-          umma_ss(tmem + sb * 128, adesc, bdesc, idesc, k ? 1u : 0u);
+          const uint64_t adesc = sdesc_kmajor_sw128(qa + (k >> 2) * (Q_BYTES / 2)) + 2 * (k & 3);
+          const uint64_t bdesc = sdesc_kmajor_sw128(kb + (k >> 2) * K_SUB) + 2 * (k & 3);
+          umma_ss(tmem + sb * BKV, adesc, bdesc, idesc_s, k ? 1u : 0u);
         }
-        any = true;
+        umma_commit(&bars->k_empty[s]);
         umma_commit(&bars->s_full[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
-      if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
+      __syncwarp();
+      any = true;
+      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+    }
+    if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
+    if (elect_one()) {
       if (ok) umma_commit(&bars->o_full);
       if (!ok && any) {
         umma_commit(&bars->drain);
         mbar_drain(&bars->drain, 0);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax (thread = query row) ----------------
+    __syncwarp();
+  } else {
+    // ---------------- softmax (warps 2-5; thread = query row = TMEM lane) ----------------
     const int q = warp & 3;
     const int row = 32 * q + lane;
     const int64_t qrow = static_cast<int64_t>(qt) * BQ + row;
@@ -212,32 +261,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int sb = j & 1;
       if (!mbar_wait(&bars->s_full[sb], (j >> 1) & 1, abort)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[128];
-      {
-        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
-        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
-        const uint32_t ta = tmem + sb * 128 + lane_off;
-        RL_TMEM_LD32(ta, s0);
-        RL_TMEM_LD32(ta + 32, s1);
-        RL_TMEM_LD32(ta + 64, s2);
-        RL_TMEM_LD32(ta + 96, s3);
-        tmem_ld_wait_regs(s);
+      uint32_t s[BKV];
+      const uint32_t ta = tmem + sb * BKV + lane_off;
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t (&sc)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]);
+        RL_TMEM_LD32(ta + 32 * c, sc);
       }
+      tmem_ld_wait_regs(s);
       // logits in log2 units, masked: key j*128 + c is visible iff key <= lim (lim < nkv); the maximum is taken on
       // the raw scores (scale_log2 > 0), masked entries set to -inf only in blocks that reach past lim
       const int64_t key0 = static_cast<int64_t>(j) * BKV;
-      float mx = -INFINITY;
-      if (key0 + BKV - 1 <= lim) {
+      if (key0 + BKV - 1 > lim) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
+        for (int c = 0; c < BKV; ++c)
           if (key0 + c > lim) s[c] = 0xFF800000u;  // -inf
-          mx = fmaxf(mx, __uint_as_float(s[c]));
-        }
+      }
+      // row maximum as 8 independent chains of three-input max (one warp per SM sub-partition has no other work to
+      // hide a 128-deep dependent chain behind)
+      float mx;
+      {
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = max3f(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]), -INFINITY);
+#pragma unroll
+        for (int c = 16; c < BKV; c += 16)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], __uint_as_float(s[c + 2 * i]), __uint_as_float(s[c + 2 * i + 1]));
+        mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       }
       mx *= p.scale_log2;
       const bool raise = mx > m_run + kTau;      // true on the first block with any visible key
@@ -263,30 +314,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // P = 2^(logit - m_run) with the hardware exp2 (P is stored as bf16 anyway), written over S
-      uint32_t pk[64];
-      float lsum = 0.0f;
+      uint32_t pk[BKV / 2];
+      float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};   // 8 independent partial sums
       if (m_run == -INFINITY) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) pk[c] = 0u;
+        for (int c = 0; c < BKV / 2; ++c) pk[c] = 0u;
       } else {
-        const float nm = -m_run, sc = p.scale_log2;
+        const float nm = -m_run, scl = p.scale_log2;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), sc, nm));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), sc, nm));
-          lsum += p0 + p1;
+        for (int c = 0; c < BKV / 2; ++c) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), scl, nm));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), scl, nm));
+          ls[c & 7] += p0 + p1;
           pk[c] = pack_bf16x2(p0, p1);
         }
       }
-      l_run += lsum;
-      {
-        uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
-        uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
-        const uint32_t ta = tmem + sb * 128 + lane_off;
-        RL_TMEM_ST32(ta, p0);
-        RL_TMEM_ST32(ta + 32, p1);
-        tmem_st_wait_regs(pk);
+      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+#pragma unroll
+      for (int c = 0; c < BKV / 64; ++c) {
+        uint32_t (&pc)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]);
+        RL_TMEM_ST32(ta + 32 * c, pc);
       }
+      tmem_st_wait_regs(pk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[sb]);
@@ -306,15 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t bits[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) bits[i] = __float_as_uint(__uint_as_float(o[8 * b + i]) * inv);
-          const uint32_t E = bfp16_block_exponent(bits);
-          uint32_t lo = 0, hi = 0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            lo |= (static_cast<uint32_t>(bfp16_quant_one(bits[i], E)) & 0xFFu) << (8 * i);
-            hi |= (static_cast<uint32_t>(bfp16_quant_one(bits[4 + i], E)) & 0xFFu) << (8 * i);
-          }
-          uint32_t w[4];
-          bfp16_decode_block(E, lo, hi, w);
+          uint32_t E, lo, hi, w[4];
+          bfp16_quant_block_fast(bits, E, lo, hi, w);
           if (qrow < p.Nq) reinterpret_cast<uint4*>(orow + 32 * c + 8 * b)[0] = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
@@ -325,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -382,15 +424,9 @@ int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64
     RL_TRY_CUDA(cudaMemset2DAsync(o, ldo * 2, 0, static_cast<size_t>(H) * HD * 2, Nq, stream));
     return RL_OK;
   }
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    RL_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kBytes));
-    attr_set[dev] = true;
-  }
   const dim3 grid(static_cast<unsigned>((Nq + BQ - 1) / BQ), static_cast<unsigned>(H));
-  attention_kernel<<<grid, kThreads, Smem::kBytes, stream>>>(mq, mk, mv, p);
+  RL_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes));
+  attention_kernel<<<grid, kThreads, kBytes, stream>>>(mq, mk, mv, p);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

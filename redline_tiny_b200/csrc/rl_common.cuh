@@ -73,13 +73,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase completes or about `hint_ns` nanoseconds pass,
+// so a waiting warp does not take issue slots from the warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase of `bar` with the given parity to complete. Gives up (returns false) when *abort is set by
-// another role, or after RL_WAIT_LIMIT_CYCLES, in which case it sets *abort and reports kErrWaitTimeout.
+// another role, or after RL_WAIT_LIMIT_CYCLES, in which case it sets *abort and reports kErrWaitTimeout. Each retry
+// sleeps in hardware for at most ~0.5 ms, after which the abort flag and the limit are checked again.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
     if (*abort) return false;
     if (clock64() - t0 > RL_WAIT_LIMIT_CYCLES) {
       *abort = 1;
@@ -139,6 +154,24 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// True in exactly one lane of the (fully active) warp: the lowest, so repeated calls elect the same thread. MMA
+// warps run their whole loop warp-wide (descriptors in uniform registers) and issue tcgen05.mma / commit from the
+// elected lane: issued from divergent lane-0 code with per-thread descriptor registers, the MMA rate dropped to
+// ~60% whenever another warp on the same SM sub-partition kept the FP32 pipe busy.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\telect.sync rx|px, %1;\n\tselp.b32 %0, 1, 0, px;\n\t}\n"
+      : "=r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
+// Bounded wait taken by a whole warp; the outcome is made warp-uniform (false if any lane gave up).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 inputs, fp32 accumulation.

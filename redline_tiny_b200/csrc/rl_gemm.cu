@@ -13,10 +13,10 @@
 //                   the decoded operand out of shared memory entirely (no write, no MMA re-read).
 // Decoding is the throughput limiter (16 weights per MMA cycle per SM), so it is spread over 4*P*G warps: P parts
 // split one stage's eight 8-deep blocks, G groups take alternate stages.
-// Warp roles: warp 0 = TMA producer + TMEM allocator, warp 1 = MMA issuer, then the expanders, then 8 epilogue
-// warps (tcgen05.ld of D, bias / SwiGLU, transposed through shared memory into row-major C). The accumulator is
-// single-buffered in TMEM (the decoded A stages take the rest), so two warps per lane quarter drain it in halves
-// and release it as soon as their last tcgen05.ld has landed, before the last stores.
+// Warp roles: warp 0 = TMA producer + TMEM allocator, warp 1 = MMA issuer (warp-wide loop, elected lane issues),
+// then the expanders, then 8 epilogue warps (tcgen05.ld of D, bias / SwiGLU, transposed through shared memory into
+// row-major C). The accumulator is single-buffered in TMEM (the decoded A stages take the rest), so two warps per
+// lane quarter drain it in halves and release it as soon as their last tcgen05.ld has landed, before the last stores.
 // The kernel is persistent: one CTA per SM walks tiles (activation-tile fastest, so the CTAs in flight share the
 // same weight columns and the whole X in L2).
 #include <cmath>
@@ -217,23 +217,26 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN);
-      int kiter = 0, it = 0;
-      bool ok = true, any = false;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
-        const int b = (C::kAccBufs == 2) ? (it & 1) : 0;
-        const int use = (C::kAccBufs == 2) ? (it >> 1) : it;
-        if (!mbar_wait(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
+    // ---------------- MMA issuer: the whole warp runs the loop, one elected lane issues ----------------
+    constexpr uint32_t idesc = idesc_bf16(BM, BN);
+    int kiter = 0, it = 0;
+    bool ok = true, any = false;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const int b = (C::kAccBufs == 2) ? (it & 1) : 0;
+      const int use = (C::kAccBufs == 2) ? (it >> 1) : it;
+      if (!mbar_wait_warp(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + b * 256;
+      for (int kt = 0; kt < KT; ++kt, ++kiter) {
+        const int s = kiter % C::kStages;
+        const uint32_t ph = (kiter / C::kStages) & 1;
+        if (!mbar_wait_warp(&bars->full[s], ph, abort) || !mbar_wait_warp(&bars->expf[s], ph, abort)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + b * 256;
-        for (int kt = 0; kt < KT; ++kt, ++kiter) {
-          const int s = kiter % C::kStages;
-          const uint32_t ph = (kiter / C::kStages) & 1;
-          if (!mbar_wait(&bars->full[s], ph, abort) || !mbar_wait(&bars->expf[s], ph, abort)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(stage_x(s)));
+        const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(stage_x(s)));
+        if (elect_one()) {
           if constexpr (V == kSmemA) {
             const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(stage_we(s)));
 #pragma unroll
@@ -245,16 +248,21 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
             for (int k = 0; k < BK / UK; ++k)
               umma_ts(d_tmem, a_tmem + k * (UK / 2), bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
           }
-          any = true;
           umma_commit(&bars->empty[s]);
         }
-        if (!ok) break;
-        umma_commit(&bars->accf[b]);
+        __syncwarp();
+        any = true;
       }
-      if (!ok && any) {  // no MMA may still be reading TMEM / shared memory when the CTA exits
+      if (!ok) break;
+      if (elect_one()) umma_commit(&bars->accf[b]);
+      __syncwarp();
+    }
+    if (!ok && any) {  // no MMA may still be reading TMEM / shared memory when the CTA exits
+      if (elect_one()) {
         umma_commit(&bars->drain);
         mbar_drain(&bars->drain, 0);
       }
+      __syncwarp();
     }
   } else if (warp < C::kEpiWarp0) {
     // ---------------- expanders: W9 (bfp16) -> bf16 A operand ----------------
