@@ -150,6 +150,44 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
   }
 }
 
+// Expander step shared by both kernels: decode this thread's weight column `row` of the 8 / P eight-deep blocks of
+// part `part` of a native W9 tile into bf16 pairs (words[4 * b + i] = K rows 8(part * 8 / P + b) + 2i, +1).
+template <int P>
+__device__ __forceinline__ void expand_w9(const uint8_t* w9, int row, int part, uint32_t (&words)[32 / P]) {
+  constexpr int BPP = 8 / P;
+  const uint2 ex = *reinterpret_cast<const uint2*>(w9 + 8192 + row * 8);
+  uint4 mq[BPP / 2];
+#pragma unroll
+  for (int j = 0; j < BPP / 2; ++j)
+    mq[j] = *reinterpret_cast<const uint4*>(w9 + ((part * (BPP / 2) + j) * 128 + row) * 16);
+#pragma unroll
+  for (int b = 0; b < BPP; ++b) {
+    const int bk = part * BPP + b;
+    const uint32_t E = __byte_perm(bk < 4 ? ex.x : ex.y, 0u, 0x4440u + (bk & 3));
+    const uint32_t u0 = (b & 1) ? mq[b >> 1].z : mq[b >> 1].x;
+    const uint32_t u1 = (b & 1) ? mq[b >> 1].w : mq[b >> 1].y;
+    uint32_t w[4];
+    bfp16_decode_block_ob(E, u0, u1, w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) words[b * 4 + i] = w[i];
+  }
+}
+
+// Store decoded words as row `row` of a 128 x 64 bf16 A tile in the 128-byte-swizzled K-major layout, then make the
+// writes visible to the tensor cores (async proxy).
+template <int P>
+__device__ __forceinline__ void store_a_sw128(uint8_t* a_tile, int row, int part, const uint32_t (&words)[32 / P]) {
+  constexpr int BPP = 8 / P;
+  uint8_t* we = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+  for (int b = 0; b < BPP; ++b) {
+    const int bk = part * BPP + b;
+    *reinterpret_cast<uint4*>(we + ((bk ^ (row & 7)) << 4)) =
+        make_uint4(words[b * 4], words[b * 4 + 1], words[b * 4 + 2], words[b * 4 + 3]);
+  }
+  fence_proxy_async_smem();
+}
+
 template <int V, int S, int G, int P>
 __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bfp16_linear_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
@@ -280,33 +318,10 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
         const int s = kiter % C::kStages;
         const uint32_t ph = (kiter / C::kStages) & 1;
         if (!mbar_wait(&bars->full[s], ph, abort)) { ok = false; break; }
-        const uint8_t* w9 = stage_w9(s);
-        const uint2 ex = *reinterpret_cast<const uint2*>(w9 + 8192 + row * 8);
-        uint4 mq[BPP / 2];
-#pragma unroll
-        for (int j = 0; j < BPP / 2; ++j)
-          mq[j] = *reinterpret_cast<const uint4*>(w9 + ((part * (BPP / 2) + j) * 128 + row) * 16);
         uint32_t words[4 * BPP];
-#pragma unroll
-        for (int b = 0; b < BPP; ++b) {
-          const int bk = part * BPP + b;
-          const uint32_t E = __byte_perm(bk < 4 ? ex.x : ex.y, 0u, 0x4440u + (bk & 3));
-          const uint32_t u0 = (b & 1) ? mq[b >> 1].z : mq[b >> 1].x;
-          const uint32_t u1 = (b & 1) ? mq[b >> 1].w : mq[b >> 1].y;
-          uint32_t w[4];
-          bfp16_decode_block_ob(E, u0, u1, w);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) words[b * 4 + i] = w[i];
-        }
+        expand_w9<P>(stage_w9(s), row, part, words);
         if constexpr (V == kSmemA) {
-          uint8_t* we = stage_we(s) + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-          for (int b = 0; b < BPP; ++b) {
-            const int bk = part * BPP + b;
-            *reinterpret_cast<uint4*>(we + ((bk ^ (row & 7)) << 4)) =
-                make_uint4(words[b * 4], words[b * 4 + 1], words[b * 4 + 2], words[b * 4 + 3]);
-          }
-          fence_proxy_async_smem();
+          store_a_sw128<P>(stage_we(s), row, part, words);
         } else {
           tc_fence_after();
           const uint32_t taddr = tmem + C::kTmemACol + s * (BK / 2) + part * (BK / 2 / P) + ((32u * q) << 16);
@@ -377,14 +392,257 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
   }
 }
 
+
+// ============================================================================================================
+// 2-SM variant: a cluster of two CTAs on neighbouring SMs computes a 256-weight-column x 256-activation-row tile
+// with tcgen05.mma.cta_group::2 (M 256 = 128 weight columns per CTA, N 256 = 128 activation rows per CTA). Each CTA
+// loads only its half of the activation tile, which halves the L2 -> SM activation traffic per FLOP, and decodes
+// its own 128-column weight tile into shared memory (the MMA's A operand, SS form), so the accumulator can be
+// double-buffered in TMEM (2 x 256 columns) and the epilogue of tile i overlaps the MMAs of tile i+1.
+// Signals: each CTA's loads complete on its own `full` barrier; both CTAs' expanders arrive on the leader's `expf`
+// (8 P arrivals per stage) and both CTAs' epilogues on the leader's `acce`; the leader's MMA commits arrive on the
+// `empty` / `accf` barriers of both CTAs.
+// ============================================================================================================
+namespace pair {
+
+constexpr int XH_BYTES = 128 * BK * 2;  // 16384: this CTA's half of the activation tile
+
+template <int S, int G, int P>
+struct Cfg {
+  static constexpr int kExpWarps = 4 * P * G;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kWarps = 2 + kExpWarps + kEpiWarps;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kEpiWarp0 = 2 + kExpWarps;
+  static constexpr int kXOff = 0;                              // S x 16 KB
+  static constexpr int kAOff = kXOff + S * XH_BYTES;           // S x 16 KB, decoded weights (SW128 K-major)
+  static constexpr int kW9Off = kAOff + S * WE_BYTES;          // S x 9216 B
+  static constexpr int kEpiOff = kW9Off + S * W9_BYTES;
+  static constexpr int kBarOff = kEpiOff + kEpiWarps * kEpiStageBytes;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOff + 256;
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(S <= 8 && G >= 1 && G <= 4 && (P == 1 || P == 2), "config");
+};
+
+template <int S, int G, int P>
+__global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
+    bfp16_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  using C = Cfg<S, G, P>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi_stage = smem + C::kEpiOff;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + C::kBarOff);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();          // 0 = leader: issues the pair's MMAs
+  const int cid = static_cast<int>(blockIdx.x >> 1), ncl = static_cast<int>(gridDim.x >> 1);
+  const int npairs = p.num_w_tiles / 2;
+  const int ntiles = p.num_x_tiles * npairs;
+
+  auto stage_x = [&](int s) { return smem + C::kXOff + s * XH_BYTES; };
+  auto stage_a = [&](int s) { return smem + C::kAOff + s * WE_BYTES; };
+  auto stage_w9 = [&](int s) { return smem + C::kW9Off + s * W9_BYTES; };
+  auto at_leader = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 0); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->expf[s], 2 * 4 * P);        // one expander group of each CTA
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->accf[b], 1);
+      mbar_init(&bars->acce[b], 2 * C::kEpiWarps);  // the epilogue warps of both CTAs
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&bars->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any signal crosses the pair
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const int KT = p.KT;
+
+  if (warp == 0) {
+    // ---------------- producer: this CTA's activation half and weight tile ----------------
+    if (lane == 0) {
+      int kiter = 0;
+      uint32_t issued = 0, last_par = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < ntiles; t += ncl) {
+        const int xt = t % p.num_x_tiles, wt = 2 * (t / p.num_x_tiles) + static_cast<int>(rank);
+        const uint8_t* wsrc = p.w9 + static_cast<int64_t>(wt) * KT * W9_BYTES;
+        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+          const int s = kiter % S;
+          const uint32_t ph = (kiter / S) & 1;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->full[s], XH_BYTES + W9_BYTES);
+          tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN + static_cast<int>(rank) * 128);
+          bulk_load(stage_w9(s), wsrc + static_cast<int64_t>(kt) * W9_BYTES, W9_BYTES, &bars->full[s]);
+          issued |= 1u << s;
+          last_par = (last_par & ~(1u << s)) | (ph << s);
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < S; ++s)
+          if (issued & (1u << s)) mbar_drain(&bars->full[s], (last_par >> s) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA): warp-wide loop, elected lane issues ----------------
+    if (rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * BM, BN);
+      int kiter = 0, it = 0;
+      bool ok = true, any = false;
+      for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
+        const int b = it & 1, use = it >> 1;
+        if (!mbar_wait_warp(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + b * 256;
+        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+          const int s = kiter % S;
+          const uint32_t ph = (kiter / S) & 1;
+          // both CTAs' expanders have decoded stage s, which they did after its loads landed
+          if (!mbar_wait_warp(&bars->expf[s], ph, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(stage_a(s)));
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(stage_x(s)));
+          if (elect_one()) {
+#pragma unroll
+            for (int k = 0; k < BK / UK; ++k)
+              umma_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            umma_commit_pair(mapa_shared(smem_u32(&bars->empty[s]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&bars->empty[s]), 1));
+          }
+          __syncwarp();
+          any = true;
+        }
+        if (!ok) break;
+        if (elect_one()) {
+          umma_commit_pair(mapa_shared(smem_u32(&bars->accf[b]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&bars->accf[b]), 1));
+        }
+        __syncwarp();
+      }
+      if (!ok && any) {  // no MMA may still be reading shared memory or TMEM when the CTAs exit
+        if (elect_one()) {
+          umma_commit_pair(mapa_shared(smem_u32(&bars->drain), 0));
+          mbar_drain(&bars->drain, 0);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp < C::kEpiWarp0) {
+    // ---------------- expanders: this CTA's W9 tile -> bf16 A tile in shared memory ----------------
+    constexpr int BPP = 8 / P;
+    const int e = warp - 2;
+    const int row = 32 * (warp & 3) + lane;
+    const int part = (e >> 2) % P;
+    const int grp = (e >> 2) / P;
+    int kiter = 0;
+    bool ok = true;
+    for (int t = cid; ok && t < ntiles; t += ncl) {
+      for (int kt = 0; kt < KT; ++kt, ++kiter) {
+        if (G > 1 && (kiter % G) != grp) continue;
+        const int s = kiter % S;
+        const uint32_t ph = (kiter / S) & 1;
+        if (!mbar_wait(&bars->full[s], ph, abort)) { ok = false; break; }
+        uint32_t words[4 * BPP];
+        expand_w9<P>(stage_w9(s), row, part, words);
+        store_a_sw128<P>(stage_a(s), row, part, words);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(at_leader(&bars->expf[s]));
+      }
+    }
+  } else {
+    // ---------------- epilogue: 8 warps, (lane quarter q, column half h) each ----------------
+    const int ew = warp - C::kEpiWarp0;
+    const int q = warp & 3;
+    const int h = ew >> 2;
+    const int row = 32 * q + lane;
+    uint8_t* st = epi_stage + ew * kEpiStageBytes;
+    constexpr int NC = BN / 2 / kChunk;
+    int it = 0;
+    bool ok = true;
+    for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
+      const int xt = t % p.num_x_tiles, wt = 2 * (t / p.num_x_tiles) + static_cast<int>(rank);
+      const int b = it & 1, use = it >> 1;
+      float bias_v = 0.0f;
+      if (p.bias) {
+        int col = row;
+        if (p.epilogue == RL_EPI_SWIGLU) col = (lane < 16 ? 0 : 64) + 16 * q + (lane & 15);
+        bias_v = bf16_bits_to_float(p.bias[static_cast<int64_t>(wt) * BM + col]);
+      }
+      if (!mbar_wait(&bars->accf[b], use & 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tbase = tmem + b * 256 + h * (BN / 2) + ((32u * q) << 16);
+      const int64_t xb = static_cast<int64_t>(xt) * BN + h * (BN / 2);
+      uint32_t ra[kChunk], rb[kChunk];
+      RL_TMEM_LD16(tbase, ra);
+      tmem_ld_wait_regs(ra);
+#pragma unroll 1
+      for (int c = 0; c < NC; c += 2) {
+        RL_TMEM_LD16(tbase + (c + 1) * kChunk, rb);
+        epilogue_chunk(p, ra, st, lane, q, wt, xb + c * kChunk, bias_v);
+        tmem_ld_wait_regs(rb);
+        if (c + 2 < NC) {
+          RL_TMEM_LD16(tbase + (c + 2) * kChunk, ra);
+        } else {  // all of buffer b is in registers: release it to the leader's MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(at_leader(&bars->acce[b]));
+        }
+        epilogue_chunk(p, rb, st, lane, q, wt, xb + (c + 1) * kChunk, bias_v);
+        if (c + 2 < NC) tmem_ld_wait_regs(ra);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while its peer may still signal its barriers or read its shared memory
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+}  // namespace pair
+
 static int g_variant = 0;  // 0 = default
 
+// Tensor map over X (M x K bf16, row-major) with boxes of 64 K x box_rows rows, 128-byte swizzle.
+inline int make_x_map(CUtensorMap* map, const uint16_t* x, int64_t M, int64_t K, int box_rows) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult cr = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), gdim, gstride, box,
+                          estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+  return RL_OK;
+}
+
 template <int V, int S, int G, int P>
-int launch(const CUtensorMap& tmap, const Params& p, cudaStream_t stream) {
+int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
   using C = Cfg<V, S, G, P>;
+  CUtensorMap tmap;
+  int st = make_x_map(&tmap, x, p.M, p.K, BN);
+  if (st != RL_OK) return st;
   static bool attr_set[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
+  RL_TRY_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     RL_TRY_CUDA(cudaFuncSetAttribute(bfp16_linear_kernel<V, S, G, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::kSmemBytes));
@@ -396,21 +654,70 @@ int launch(const CUtensorMap& tmap, const Params& p, cudaStream_t stream) {
   return RL_OK;
 }
 
-// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S); 0 = default.
-int dispatch(int code, const CUtensorMap& tmap, const Params& p, cudaStream_t stream) {
+// Pair kernel: clusters of two CTAs; the grid is as many clusters as can be resident at once (at most one per pair
+// tile), each walking pair tiles with stride = number of clusters.
+template <int S, int G, int P>
+int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
+  using C = pair::Cfg<S, G, P>;
+  auto kernel = pair::bfp16_linear_pair_kernel<S, G, P>;
+  CUtensorMap tmap;
+  int st = make_x_map(&tmap, x, p.M, p.K, 128);
+  if (st != RL_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2 * 1);
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  RL_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(RL_ERR_CUDA, "rl_linear_bfp16: device index %d", dev);
+  if (max_clusters[dev] == 0) {
+    RL_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    int n = 0;
+    RL_TRY_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+    if (n <= 0) return fail(RL_ERR_UNSUPPORTED, "rl_linear_bfp16: no CTA pair fits on this device");
+    max_clusters[dev] = n;
+  }
+  const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2);
+  const int nclusters = ntiles < max_clusters[dev] ? ntiles : max_clusters[dev];
+  cfg.gridDim = dim3(2 * nclusters);
+  RL_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p));
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S; V = 3 is the 2-SM
+// pair kernel); 0 = default: the pair kernel when N is a multiple of 256, else the 1-SM kernel with A in TMEM.
+int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) {
+  const bool pairable = p.num_w_tiles % 2 == 0;
+  if (code == 0) code = pairable ? 1335 : 1325;
   switch (code) {
     case 1:
-    case 1213: return launch<kSmemA, 3, 2, 1>(tmap, p, stream);
-    case 1125: return launch<kTmemA, 5, 1, 1>(tmap, p, stream);
-    case 0:
+    case 1213: return launch<kSmemA, 3, 2, 1>(x, p, stream);
+    case 1125: return launch<kTmemA, 5, 1, 1>(x, p, stream);
+    case 1225: return launch<kTmemA, 5, 2, 1>(x, p, stream);
     case 2:
-    case 1225: return launch<kTmemA, 5, 2, 1>(tmap, p, stream);
-    case 1325: return launch<kTmemA, 5, 3, 1>(tmap, p, stream);
-    case 2125: return launch<kTmemA, 5, 1, 2>(tmap, p, stream);
-    case 2225: return launch<kTmemA, 5, 2, 2>(tmap, p, stream);
-    case 2224: return launch<kTmemA, 4, 2, 2>(tmap, p, stream);
-    default: return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
+    case 1325: return launch<kTmemA, 5, 3, 1>(x, p, stream);
+    case 2125: return launch<kTmemA, 5, 1, 2>(x, p, stream);
+    case 2225: return launch<kTmemA, 5, 2, 2>(x, p, stream);
+    case 2224: return launch<kTmemA, 4, 2, 2>(x, p, stream);
+    default: break;
   }
+  if (code == 3 || code == 1335 || code == 1235 || code == 2235) {
+    if (!pairable) return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: the pair kernel needs N %% 256 == 0");
+    if (code == 1235) return launch_pair<5, 2, 1>(x, p, stream);
+    if (code == 2235) return launch_pair<5, 2, 2>(x, p, stream);
+    return launch_pair<5, 3, 1>(x, p, stream);
+  }
+  return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
 }
 
 }  // namespace gemm
@@ -443,19 +750,6 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
   RL_REQUIRE(K <= (int64_t)1 << 31 && M < ((int64_t)1 << 31), RL_ERR_ARGUMENT, "rl_linear_bfp16: size too large");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_linear_bfp16: needs an sm_100 device");
   if (M == 0) return RL_OK;
-  EncodeTiledFn enc = encode_tiled();
-  RL_REQUIRE(enc != nullptr, RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled unavailable");
-
-  CUtensorMap tmap;
-  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(K) * 2};
-  const cuuint32_t box[2] = {BK, BN};
-  const cuuint32_t estride[2] = {1, 1};
-  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), gdim, gstride, box,
-                    estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  RL_REQUIRE(cr == CUDA_SUCCESS, RL_ERR_CUDA, "rl_linear_bfp16: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-
   Params p;
   p.w9 = w_native;
   p.bias = (epilogue == RL_EPI_NONE) ? nullptr : bias;
@@ -469,7 +763,7 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
   p.num_w_tiles = static_cast<int>(N / BM);
   p.num_tiles = p.num_x_tiles * p.num_w_tiles;
   p.KT = static_cast<int>(K / BK);
-  return dispatch(g_variant, tmap, p, stream);
+  return dispatch(g_variant, x, p, stream);
 }
 
 }  // extern "C"
