@@ -194,8 +194,10 @@ int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64
                  int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, int64_t ldo,
                  rl_stream_t stream);
 
-/* GEMM kernel variant for tests and benchmarks: 0 = default (= 2), 1 = weights decoded into shared memory (MMA A
- * operand from shared memory), 2 = weights decoded into tensor memory (A from TMEM); tuning codes
+/* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
+ * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
+ * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel
+ * (tcgen05.mma cta_group::2 over a cluster of two CTAs) with A in shared memory / TMEM; tuning codes
  * 1000*P + 100*G + 10*V + S also select the decode split and the pipeline depth. Returns the previous value. */
 int rl_set_gemm_variant(int variant);
 

@@ -407,27 +407,33 @@ namespace pair {
 
 constexpr int XH_BYTES = 128 * BK * 2;  // 16384: this CTA's half of the activation tile
 
-template <int S, int G, int P>
+// V = kSmemA: decoded weights in shared memory (SS MMA), accumulator double-buffered in TMEM (2 x 256 columns).
+// V = kTmemA: decoded weights in TMEM (TS MMA, 32 columns per stage after a single 256-column accumulator), which
+//             frees 16 KB of shared memory per stage for a deeper pipeline.
+template <int V, int S, int G, int P>
 struct Cfg {
   static constexpr int kExpWarps = 4 * P * G;
   static constexpr int kEpiWarps = 8;
   static constexpr int kWarps = 2 + kExpWarps + kEpiWarps;
   static constexpr int kThreads = 32 * kWarps;
   static constexpr int kEpiWarp0 = 2 + kExpWarps;
-  static constexpr int kXOff = 0;                              // S x 16 KB
-  static constexpr int kAOff = kXOff + S * XH_BYTES;           // S x 16 KB, decoded weights (SW128 K-major)
-  static constexpr int kW9Off = kAOff + S * WE_BYTES;          // S x 9216 B
+  static constexpr int kXOff = 0;                                            // S x 16 KB
+  static constexpr int kAOff = kXOff + S * XH_BYTES;                         // SS: S x 16 KB (SW128 K-major)
+  static constexpr int kW9Off = kAOff + (V == kSmemA ? S * WE_BYTES : 0);    // S x 9216 B
   static constexpr int kEpiOff = kW9Off + S * W9_BYTES;
   static constexpr int kBarOff = kEpiOff + kEpiWarps * kEpiStageBytes;
+  static constexpr int kAccBufs = V == kSmemA ? 2 : 1;
+  static constexpr int kTmemACol = 256;                                      // TS: A stages after the accumulator
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOff + 256;
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(V == kSmemA || 256 + S * (BK / 2) <= 512, "TMEM: accumulator + A stages");
   static_assert(S <= 8 && G >= 1 && G <= 4 && (P == 1 || P == 2), "config");
 };
 
-template <int S, int G, int P>
-__global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
+template <int V, int S, int G, int P>
+__global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bfp16_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
-  using C = Cfg<S, G, P>;
+  using C = Cfg<V, S, G, P>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_stage = smem + C::kEpiOff;
@@ -503,7 +509,7 @@ __global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
       int kiter = 0, it = 0;
       bool ok = true, any = false;
       for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
-        const int b = it & 1, use = it >> 1;
+        const int b = C::kAccBufs == 2 ? (it & 1) : 0, use = C::kAccBufs == 2 ? (it >> 1) : it;
         if (!mbar_wait_warp(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * 256;
@@ -513,12 +519,19 @@ __global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
           // both CTAs' expanders have decoded stage s, which they did after its loads landed
           if (!mbar_wait_warp(&bars->expf[s], ph, abort)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(stage_a(s)));
           const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(stage_x(s)));
           if (elect_one()) {
+            if constexpr (V == kSmemA) {
+              const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(stage_a(s)));
 #pragma unroll
-            for (int k = 0; k < BK / UK; ++k)
-              umma_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              for (int k = 0; k < BK / UK; ++k)
+                umma_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            } else {
+              const uint32_t a_tmem = tmem + C::kTmemACol + s * (BK / 2);
+#pragma unroll
+              for (int k = 0; k < BK / UK; ++k)
+                umma_ts_pair(d_tmem, a_tmem + k * (UK / 2), bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            }
             umma_commit_pair(mapa_shared(smem_u32(&bars->empty[s]), 0));
             umma_commit_pair(mapa_shared(smem_u32(&bars->empty[s]), 1));
           }
@@ -557,7 +570,19 @@ __global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
         if (!mbar_wait(&bars->full[s], ph, abort)) { ok = false; break; }
         uint32_t words[4 * BPP];
         expand_w9<P>(stage_w9(s), row, part, words);
-        store_a_sw128<P>(stage_a(s), row, part, words);
+        if constexpr (V == kSmemA) {
+          store_a_sw128<P>(stage_a(s), row, part, words);
+        } else {
+          tc_fence_after();
+          const uint32_t taddr = tmem + C::kTmemACol + s * (BK / 2) + part * (BK / 2 / P) + ((32u * (warp & 3)) << 16);
+          if constexpr (P == 1) {
+            RL_TMEM_ST32(taddr, words);
+          } else {
+            RL_TMEM_ST16(taddr, words);
+          }
+          tmem_st_wait_regs(words);
+          tc_fence_before();
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(at_leader(&bars->expf[s]));
       }
@@ -574,7 +599,7 @@ __global__ void __launch_bounds__(Cfg<S, G, P>::kThreads, 1)
     bool ok = true;
     for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
       const int xt = t % p.num_x_tiles, wt = 2 * (t / p.num_x_tiles) + static_cast<int>(rank);
-      const int b = it & 1, use = it >> 1;
+      const int b = C::kAccBufs == 2 ? (it & 1) : 0, use = C::kAccBufs == 2 ? (it >> 1) : it;
       float bias_v = 0.0f;
       if (p.bias) {
         int col = row;
@@ -656,10 +681,10 @@ int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
 
 // Pair kernel: clusters of two CTAs; the grid is as many clusters as can be resident at once (at most one per pair
 // tile), each walking pair tiles with stride = number of clusters.
-template <int S, int G, int P>
+template <int V, int S, int G, int P>
 int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
-  using C = pair::Cfg<S, G, P>;
-  auto kernel = pair::bfp16_linear_pair_kernel<S, G, P>;
+  using C = pair::Cfg<V, S, G, P>;
+  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P>;
   CUtensorMap tmap;
   int st = make_x_map(&tmap, x, p.M, p.K, 128);
   if (st != RL_OK) return st;
@@ -694,11 +719,12 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   return RL_OK;
 }
 
-// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S; V = 3 is the 2-SM
-// pair kernel); 0 = default: the pair kernel when N is a multiple of 256, else the 1-SM kernel with A in TMEM.
+// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S; V = 3 / 4 are the
+// 2-SM pair kernel with A in shared memory / TMEM); 0 = default: the pair kernel with A in TMEM (8 stages, decode
+// split in two parts x two groups) when N is a multiple of 256, else the 1-SM kernel with A in TMEM.
 int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) {
   const bool pairable = p.num_w_tiles % 2 == 0;
-  if (code == 0) code = pairable ? 1335 : 1325;
+  if (code == 0) code = pairable ? 2248 : 1325;
   switch (code) {
     case 1:
     case 1213: return launch<kSmemA, 3, 2, 1>(x, p, stream);
@@ -711,11 +737,18 @@ int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) 
     case 2224: return launch<kTmemA, 4, 2, 2>(x, p, stream);
     default: break;
   }
-  if (code == 3 || code == 1335 || code == 1235 || code == 2235) {
+  if (code == 3 || code == 4 || code == 1335 || code == 1235 || code == 2235 || code == 1348 || code == 1448 ||
+      code == 2248) {
     if (!pairable) return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: the pair kernel needs N %% 256 == 0");
-    if (code == 1235) return launch_pair<5, 2, 1>(x, p, stream);
-    if (code == 2235) return launch_pair<5, 2, 2>(x, p, stream);
-    return launch_pair<5, 3, 1>(x, p, stream);
+    switch (code) {
+      case 1235: return launch_pair<kSmemA, 5, 2, 1>(x, p, stream);
+      case 2235: return launch_pair<kSmemA, 5, 2, 2>(x, p, stream);
+      case 4:
+      case 1348: return launch_pair<kTmemA, 8, 3, 1>(x, p, stream);
+      case 1448: return launch_pair<kTmemA, 8, 4, 1>(x, p, stream);
+      case 2248: return launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
+      default: return launch_pair<kSmemA, 5, 3, 1>(x, p, stream);
+    }
   }
   return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
 }

@@ -14,7 +14,7 @@ from oracle import bfp16_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = [1, 2, 3]   # 1-SM with A in shared memory, 1-SM with A in TMEM, 2-SM pair (needs N % 256 == 0)
+VARIANTS = [1, 2, 3, 4]   # 1-SM with A in shared memory / TMEM, 2-SM pair with A in shared memory / TMEM (pairs need N % 256 == 0)
 BF16_OUT_TOL = 2e-3 + 2.0 ** -8
 
 
@@ -35,7 +35,7 @@ def _case(M, K, N, seed=0, bias=True):
 
 
 def _skip_unpairable(variant, N):
-    if variant == 3 and N % 256:
+    if variant in (3, 4) and N % 256:
         pytest.skip("the pair kernel covers N % 256 == 0 (others use the 1-SM kernel)")
 
 
