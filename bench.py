@@ -34,7 +34,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-rows", type=int, default=128, help="reference arm: X rows per step (bounded sample)")
@@ -435,7 +435,7 @@ def run_ours(args, ws, rank, local):
                       "l2": "inputs rotate over 3 sets (X + packed W + out = 176 MB per step > 126 MB L2)"},
            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": traffic,
-                        "kernel": "bfp16_linear_kernel", "peak_kind": f"{pk_kind} bf16 dense (burst)",
+                        "kernel": "bfp16_linear_pair_kernel", "peak_kind": f"{pk_kind} bf16 dense (burst)",
                         "algorithmic_flop_per_launch": FLOP},
            "clocks": clk.summary(),
            "e2e": {"value": FLOP * e2e_steps * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
