@@ -113,7 +113,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// TMA and bulk copies (loads only; never with cluster multicast)
+// TMA and bulk copies (loads only, each into the issuing CTA's own shared memory)
 // ------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
