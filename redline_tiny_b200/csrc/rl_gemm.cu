@@ -119,8 +119,13 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
   } else if (!p.out_f32) {
     uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
 #pragma unroll
-    for (int j = 0; j < kChunk; ++j)
-      s16[j * 32 + lane] = static_cast<uint16_t>(float_to_bf16_bits(__uint_as_float(r[j]) + bias_v));
+    for (int j = 0; j < kChunk; j += 2) {
+      uint32_t pr;   // rows j (low half) and j + 1 (high half), rounded to nearest even in one instruction
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(__uint_as_float(r[j + 1]) + bias_v),
+          "f"(__uint_as_float(r[j]) + bias_v));
+      s16[j * 32 + lane] = static_cast<uint16_t>(pr);
+      s16[(j + 1) * 32 + lane] = static_cast<uint16_t>(pr >> 16);
+    }
     __syncwarp();
     uint16_t* outp = static_cast<uint16_t*>(p.out);
 #pragma unroll
