@@ -146,38 +146,62 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16
                                                                     const float* __restrict__ wk, int64_t M, int H,
                                                                     float eps, uint16_t* __restrict__ q,
                                                                     uint16_t* __restrict__ k) {
+  // one warp per token; a half-warp per head (lane & 15 = 16-byte chunk of 8 dims = 4 RoPE pairs), so each step
+  // covers two heads with fully coalesced 256-byte loads and a 16-lane (4-level) sum of squares
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hh = lane >> 4, c = lane & 15;
   const int64_t ld = static_cast<int64_t>(3) * H * 128;
-  const float4 w_q = __ldg(reinterpret_cast<const float4*>(wq) + lane);
-  const float4 w_k = __ldg(reinterpret_cast<const float4*>(wk) + lane);
+  const float4 wq0 = __ldg(reinterpret_cast<const float4*>(wq) + 2 * c), wq1 = __ldg(reinterpret_cast<const float4*>(wq) + 2 * c + 1);
+  const float4 wk0 = __ldg(reinterpret_cast<const float4*>(wk) + 2 * c), wk1 = __ldg(reinterpret_cast<const float4*>(wk) + 2 * c + 1);
   for (int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + warp; m < M; m += static_cast<int64_t>(gridDim.x) * kWarps) {
-    const float4 c = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + lane);  // (cos, sin) of pairs 2l, 2l+1
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + 2 * c);      // (cos, sin) of pairs 4c, 4c+1
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + 2 * c + 1);  // pairs 4c+2, 4c+3
     const uint16_t* row = qkv + m * ld;
-#pragma unroll 2
-    for (int u = 0; u < 2 * H; ++u) {                 // u < H: q head u; else k head u - H
-      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(row + static_cast<int64_t>(u) * 128) + lane);
-      const float v0 = __uint_as_float(raw.x << 16), v1 = __uint_as_float(raw.x & 0xFFFF0000u);
-      const float v2 = __uint_as_float(raw.y << 16), v3 = __uint_as_float(raw.y & 0xFFFF0000u);
-      const float ss = warp_sum(v0 * v0 + v1 * v1 + v2 * v2 + v3 * v3);
+#pragma unroll 4
+    for (int i = 0; i < H; ++i) {                     // heads u = 2i + hh: u < H is q head u, else k head u - H
+      const int u = 2 * i + hh;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row + static_cast<int64_t>(u) * 128) + c);
+      float v[8];
+      const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = __uint_as_float(rw[j] << 16);
+        v[2 * j + 1] = __uint_as_float(rw[j] & 0xFFFF0000u);
+      }
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
-      const float4 w = u < H ? w_q : w_k;
-      const float n0 = v0 * inv * w.x, n1 = v1 * inv * w.y, n2 = v2 * inv * w.z, n3 = v3 * inv * w.w;
-      const float o0 = n0 * c.x - n1 * c.y, o1 = n0 * c.y + n1 * c.x;
-      const float o2 = n2 * c.z - n3 * c.w, o3 = n2 * c.w + n3 * c.z;
-      uint16_t* dst = (u < H ? q + (static_cast<int64_t>(u) * M + m) * 128 : k + (static_cast<int64_t>(u - H) * M + m) * 128);
-      reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack_bf16x2_rn(o0, o1), pack_bf16x2_rn(o2, o3));
+      const bool isq = u < H;
+      const float w[8] = {isq ? wq0.x : wk0.x, isq ? wq0.y : wk0.y, isq ? wq0.z : wk0.z, isq ? wq0.w : wk0.w,
+                          isq ? wq1.x : wk1.x, isq ? wq1.y : wk1.y, isq ? wq1.z : wk1.z, isq ? wq1.w : wk1.w};
+      const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      uint32_t out[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float n0 = v[2 * j] * inv * w[2 * j], n1 = v[2 * j + 1] * inv * w[2 * j + 1];
+        const float co = cc[2 * j], si = cc[2 * j + 1];
+        out[j] = pack_bf16x2_rn(n0 * co - n1 * si, n0 * si + n1 * co);
+      }
+      uint16_t* dst = isq ? q + (static_cast<int64_t>(u) * M + m) * 128 : k + (static_cast<int64_t>(u - H) * M + m) * 128;
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(out[0], out[1], out[2], out[3]);
     }
   }
 }
 
-// V (the third third of qkv) -> vt (H, 128, ldv): 64 tokens x 128 dims per CTA, 16-byte loads and stores through a
-// padded shared tile [dim][token].
+// V (token-major, 128 dims per head) -> V^T (head, dim, token), 64 tokens x 128 dims per CTA through shared memory.
+// The tile is [128 dims][64 tokens] of bf16 with the 16-byte chunk index of a row XOR-ed with (dim / 8) & 7, so the
+// transposing 2-byte stores (16 dim groups per warp) spread over 8 bank groups and the row reads stay 16-byte
+// vectors.
 __global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t* __restrict__ qkv, int64_t M, int H,
                                                                  int64_t ldv, uint16_t* __restrict__ vt) {
-  __shared__ __align__(16) uint16_t tile[128][64 + 8];
+  __shared__ __align__(16) uint16_t tile[128 * 64];
   const int64_t ld = static_cast<int64_t>(3) * H * 128;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64;
   const int h = blockIdx.y;
+  auto at = [](int d, int t) { return d * 64 + ((((t >> 3) ^ (d >> 3)) & 7) << 3) + (t & 7); };
 #pragma unroll
   for (int it = 0; it < 4; ++it) {                    // 64 tokens x 16 chunks of 8 dims
     const int cid = threadIdx.x + it * kThreads;
@@ -188,8 +212,8 @@ __global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t*
     const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      tile[8 * dg + 2 * i][t] = static_cast<uint16_t>(wv[i]);
-      tile[8 * dg + 2 * i + 1][t] = static_cast<uint16_t>(wv[i] >> 16);
+      tile[at(8 * dg + 2 * i, t)] = static_cast<uint16_t>(wv[i]);
+      tile[at(8 * dg + 2 * i + 1, t)] = static_cast<uint16_t>(wv[i] >> 16);
     }
   }
   __syncthreads();
@@ -200,7 +224,7 @@ __global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t*
     const int64_t m = m0 + 8 * tc;
     if (m < ldv)
       *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(h) * 128 + d) * ldv + m) =
-          *reinterpret_cast<const uint4*>(&tile[d][8 * tc]);
+          *reinterpret_cast<const uint4*>(&tile[at(d, 8 * tc)]);
   }
 }
 
