@@ -278,7 +278,7 @@ def measure_configs(dev, stream, ws, seed):
                           "TFLOP_per_step": cfg.flop_per_step() / 1e12, "weights_GB": 5.44}
     del model
     torch.cuda.empty_cache()
-    if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1 (NCCL all-reduce of fp32 partials)
+    if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1 (NCCL all-reduce of bf16 partials)
         import torch.distributed as dist
         rank = dist.get_rank()
         w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
@@ -291,7 +291,8 @@ def measure_configs(dev, stream, ws, seed):
         dist.barrier()
         ms = _event_ms(lambda: tp_model.denoise_step(lat1, txt1, 3), 3, 2, stream)
         out[f"C4_dit_step_tp{ws}"] = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
-                                      "all_reduce_per_step": 2 * cfg.blocks, "all_reduce_bytes": cfg.M * cfg.hidden * 4}
+                                      "all_reduce_per_step": 2 * cfg.blocks, "all_reduce_bytes": cfg.M * cfg.hidden * 2,
+                                      "all_reduce_dtype": "bf16"}
         del tp_model
         torch.cuda.empty_cache()
     return out

@@ -90,35 +90,32 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
     const float mean = s1 / static_cast<float>(D);
     const float var = fmaxf(s2 / static_cast<float>(D) - mean * mean, 0.0f);
     const float rstd = 1.0f / sqrtf(var + eps);
-    // pass 2: y = (x' - mean) * rstd * sc, rounded to bfp16 blocks of 8 along the row
+    // pass 2: y = (x' - mean) * rstd * sc, rounded to bfp16 blocks of 8 along the row; x' is read back from xo
+    // when the caller asked for it (each lane reads the blocks it wrote itself in pass 1)
     for (int64_t kb = lane; kb < KB; kb += 32) {
-      float xf[8], bf[8], gf[8], sf[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
+      float sf[8], v[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(sc) + kb), sf);
-      load_branch(br, br_f32, r, D, kb, bf);
-      if (br_f32) {
+      if (xo) {
+        unpack8(reinterpret_cast<const uint4*>(xo + r * D)[kb], v);
+      } else {
+        float xf[8], bf[8], gf[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
+        load_branch(br, br_f32, r, D, kb, bf);
+        if (br_f32) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
+          for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          v[i] = bf16_bits_to_float(float_to_bf16_bits(__fadd_rn(xf[i], __fmul_rn(gf[i], bf[i]))));
       }
       uint32_t bits[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float v = bf16_bits_to_float(float_to_bf16_bits(__fadd_rn(xf[i], __fmul_rn(gf[i], bf[i]))));
-        bits[i] = __float_as_uint((v - mean) * rstd * sf[i]);
-      }
-      const uint32_t E = bfp16_block_exponent(bits);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        lo |= (static_cast<uint32_t>(bfp16_quant_one(bits[i], E)) & 0xFFu) << (8 * i);
-        hi |= (static_cast<uint32_t>(bfp16_quant_one(bits[4 + i], E)) & 0xFFu) << (8 * i);
-      }
-      if (y_dq) {
-        uint32_t w[4];
-        bfp16_decode_block(E, lo, hi, w);
-        reinterpret_cast<uint4*>(y_dq + r * D)[kb] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+      for (int i = 0; i < 8; ++i) bits[i] = __float_as_uint((v[i] - mean) * rstd * sf[i]);
+      uint32_t E, lo, hi, wq[4];
+      bfp16_quant_block_fast(bits, E, lo, hi, wq);
+      if (y_dq) reinterpret_cast<uint4*>(y_dq + r * D)[kb] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
       if (y_q) {
         uint8_t* dst = y_q + (r * KB + kb) * 9;
         dst[0] = static_cast<uint8_t>(E);

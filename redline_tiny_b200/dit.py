@@ -110,10 +110,14 @@ class DiT:
     """Resident packed weights + preallocated activations for one denoise step of config `cfg` on one GPU.
 
     tp = (rank, world, group): tensor-parallel over `world` GPUs with `weights` already sharded by shard_weights;
-    the out-projection and down-projection write fp32 partial sums that one NCCL all-reduce each per block adds up
-    (two per block, the block being two sequential sublayers), and the residual / LayerNorm run replicated."""
+    the out-projection and down-projection write partial sums that one NCCL all-reduce each adds up (two per block,
+    the block being two sequential sublayers), and the residual / LayerNorm run replicated. reduce_dtype: "bf16"
+    (default; the partials are rounded to bf16 before the sum, half the bytes on NVLink) or "fp32"."""
 
-    def __init__(self, cfg, weights, device="cuda", tp=None):
+    def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="bf16"):
+        if reduce_dtype not in ("bf16", "fp32"):
+            raise ValueError(f"reduce_dtype must be 'bf16' or 'fp32', not {reduce_dtype!r}")
+        self.reduce_f32 = reduce_dtype == "fp32"
         self.cfg = cfg
         dev = torch.device(device)
         self.dev = dev
@@ -148,7 +152,7 @@ class DiT:
         self.vt = torch.empty(H, 128, self.ldv, **bf)
         self.o = torch.empty(M, H * HEAD_DIM, **bf)
         self.c = torch.empty(M, D, **bf)
-        self.c32 = torch.empty(M, D, dtype=torch.float32, device=dev) if tp else None
+        self.c32 = torch.empty(M, D, dtype=torch.float32, device=dev) if tp and self.reduce_f32 else None
         self.h = torch.empty(M, F, **bf)
         self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
         self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
@@ -192,14 +196,18 @@ class DiT:
         self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
 
     def _branch(self, x, w):
-        """The out / down projection: bf16 on one GPU; fp32 partial sums all-reduced across the TP group."""
+        """The out / down projection: bf16 on one GPU; partial sums all-reduced across the TP group."""
         if not self.tp:
             self._linear(x, w, self.c)
             return self.c
-        self._linear(x, w, self.c32, out_dtype=L.RL_F32)
         import torch.distributed as dist
-        dist.all_reduce(self.c32, group=self.tp[2])
-        return self.c32
+        if self.reduce_f32:
+            self._linear(x, w, self.c32, out_dtype=L.RL_F32)
+            dist.all_reduce(self.c32, group=self.tp[2])
+            return self.c32
+        self._linear(x, w, self.c)
+        dist.all_reduce(self.c, group=self.tp[2])
+        return self.c
 
     def block(self, i, last=False):
         cfg, b = self.cfg, self.blocks[i]

@@ -1,5 +1,5 @@
-"""Tensor-parallel DiT on 2 GPUs (one process per GPU, NCCL all-reduce of the fp32 partial projections) against
-the unsharded CPU oracle: velocity cosine >= 0.999. Needs two GPUs; skipped otherwise."""
+"""Tensor-parallel DiT on 2 GPUs (one process per GPU, NCCL all-reduce of the partial projections in bf16 and in
+fp32) against the unsharded CPU oracle: velocity cosine >= 0.999. Needs two GPUs; skipped otherwise."""
 
 import os
 
@@ -8,8 +8,10 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+_PORTS = iter(range(29800 + (os.getpid() % 40) * 10, 29800 + (os.getpid() % 40) * 10 + 10))
 
-def _worker(rank, world, port, q, blocks_cfg):
+
+def _worker(rank, world, port, q, blocks_cfg, reduce_dtype):
     import datetime
     import torch
     import torch.distributed as dist
@@ -22,7 +24,7 @@ def _worker(rank, world, port, q, blocks_cfg):
         cfg = dit.DiTConfig(**blocks_cfg)
         w = dit.random_weights(cfg, seed=5, device=f"cuda:{rank}")
         model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, world), device=f"cuda:{rank}",
-                        tp=(rank, world, dist.group.WORLD))
+                        tp=(rank, world, dist.group.WORLD), reduce_dtype=reduce_dtype)
         rng = np.random.default_rng(5)
         lat = rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32)
         txt = rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32)
@@ -41,17 +43,18 @@ def _worker(rank, world, port, q, blocks_cfg):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("reduce_dtype", ["bf16", "fp32"])
 @pytest.mark.parametrize("blocks_cfg", [dict(hidden=256, heads=2, ffn=512, blocks=2, text=64, image=192, grid=(12, 16)),
                                         dict(blocks=1)])
-def test_tp2_dit_matches_oracle(blocks_cfg):
+def test_tp2_dit_matches_oracle(blocks_cfg, reduce_dtype):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29800 + os.getpid() % 100
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, blocks_cfg)) for r in range(2)]
+    port = next(_PORTS)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, blocks_cfg, reduce_dtype)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
