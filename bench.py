@@ -424,7 +424,11 @@ def run_ours(args, ws, rank, local):
         return
 
     pk, pk_kind = peaks()
-    peak = pk["bf16_tflops"]
+    clocks = clk.summary()
+    # a GEMM timed over a long loop runs under the power cap: compare it with the measured sustained peak when the
+    # sampled clocks show the cap, with the burst peak otherwise (both fractions are reported)
+    capped = "sw_power_cap" in clocks.get("reasons", [])
+    peak = pk["bf16_tflops_sustained"] if capped else pk["bf16_tflops"]
     achieved = FLOP / (gemm_ms * 1e-3) / 1e12
     traffic = ncu_traffic()
     value = FLOP * args.steps * ws / (ms * 1e-3) / 1e12
@@ -436,9 +440,12 @@ def run_ours(args, ws, rank, local):
                       "l2": "inputs rotate over 3 sets (X + packed W + out = 176 MB per step > 126 MB L2)"},
            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": traffic,
-                        "kernel": "bfp16_linear_pair_kernel", "peak_kind": f"{pk_kind} bf16 dense (burst)",
+                        "kernel": "bfp16_linear_pair_kernel",
+                        "peak_kind": f"{pk_kind} bf16 dense ({'sustained, power cap seen' if capped else 'burst'})",
+                        "frac_of_burst_peak": achieved / pk["bf16_tflops"],
+                        "frac_of_sustained_peak": achieved / pk["bf16_tflops_sustained"],
                         "algorithmic_flop_per_launch": FLOP},
-           "clocks": clk.summary(),
+           "clocks": clocks,
            "e2e": {"value": FLOP * e2e_steps * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
            "gpu_launches": 2 * args.steps,
