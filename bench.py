@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
 
-Workload (the DiT FFN up-projection; one per GPU, data-parallel): X[4352, 3072] ~ N(0,1) bf16,
+Workload (config 1, the DiT FFN up-projection; one per GPU, data-parallel): X[4352, 3072] ~ N(0,1) bf16,
 W[3072, 12288] ~ N(0, 0.02) packed to bfp16, bias ~ N(0, 0.01); one step = quantise X to bfp16 (bit-exact with the
 reference) + the packed-weight GEMM with the bias epilogue, fp32 accumulation, bf16 out. The metric is the
 reference's headline "bfp16 GEMM TFLOP/s" (2*M*N*K per step, quantiser time included). Inputs rotate over three
@@ -209,7 +209,7 @@ def _event_ms(fn, n, w, stream):
 
 
 def measure_configs(dev, stream, ws, seed):
-    """The other BASELINE configs on this GPU (every rank runs its own copy: data-parallel), CUDA-event timed.
+    """The other benchmark configs (2-5) on this GPU (every rank runs its own copy: data-parallel), CUDA-event timed.
     Inputs are seeded synthetic tensors of the configs' shapes; weights N(0, 0.02)."""
     import math
     import torch

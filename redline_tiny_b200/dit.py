@@ -76,7 +76,7 @@ def random_weights(cfg, seed=0, device="cuda"):
 
 
 def shard_weights(weights, cfg, rank, world):
-    """Tensor-parallel shard `rank` of `world` (SURVEY 8e-ii layout): QKV columns and out-projection rows of this
+    """Tensor-parallel shard `rank` of `world`: QKV columns and out-projection rows of this
     rank's heads (each head's q, k and v stay together), gate / proj units and down-projection rows of this rank's
     FFN units (interleaved 128-column tiles stay whole). Norm and host weights are replicated."""
     H, F, D = cfg.heads, cfg.ffn, cfg.hidden
@@ -126,18 +126,19 @@ class DiT:
         D, M = cfg.hidden, cfg.M
         H, F = cfg.heads // world, cfg.ffn // world
         self.heads_local = H
-        pw = ops.PackedWeight.from_float
+        def pw(t, swiglu=False):     # float B (packed here) or an already resident PackedWeight (weights.load_packed)
+            return t if isinstance(t, ops.PackedWeight) else ops.PackedWeight.from_float(t.to(dev), swiglu=swiglu)
+
         self.blocks = []
         for b in weights["blocks"]:
+            up = b["up"] if "up" in b else interleave_up_torch(b["gate"], b["proj"])
             self.blocks.append({
-                "qkv": pw(b["qkv"].to(dev)), "o": pw(b["o"].to(dev)),
-                "up": pw(interleave_up_torch(b["gate"], b["proj"]).to(dev), swiglu=True),
-                "down": pw(b["down"].to(dev)),
+                "qkv": pw(b["qkv"]), "o": pw(b["o"]), "up": pw(up, swiglu=True), "down": pw(b["down"]),
                 "wq": (b["norm_q"] * C_LOG2).to(dev).float().contiguous(),
                 "wk": b["norm_k"].to(dev).float().contiguous(),
             })
-        self.img_in = pw(weights["img_in"].to(dev))
-        self.proj_out = pw(weights["proj_out"].to(dev))
+        self.img_in = pw(weights["img_in"])
+        self.proj_out = pw(weights["proj_out"])
         self.host = weights["host"]
         pad, shapes = HG.joint_layout(np.zeros(cfg.text, bool), n_target=cfg.image, grid=cfg.grid)
         self.rope_cs = torch.from_numpy(HG.rope(pad, shapes)).to(dev).contiguous()     # (M, 64, 2)

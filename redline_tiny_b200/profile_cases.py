@@ -1,4 +1,4 @@
-"""Run one hot-path kernel (or one DiT block) on its BASELINE shape a few times - the target of ncu captures.
+"""Run one hot-path kernel (or one DiT block) on its benchmark-config shape a few times - the target of ncu captures.
 
     python -m redline_tiny_b200.profile_cases <case> [--iters N]
 

@@ -87,6 +87,6 @@ def test_attention_fully_masked_rows(env):
 
 
 def test_attention_config3_size(env):
-    """BASELINE config 3 attention: 24 heads x 4352 tokens (256 text + 4096 image), non-causal; heads 0 and 23
+    """Benchmark config 3 attention: 24 heads x 4352 tokens (256 text + 4096 image), non-causal; heads 0 and 23
     checked against float64 (run_attn.py:203 checks heads {0, H-1} the same way)."""
     _run(env, 24, 4352, 4352, seed=7, heads=[0, 23])

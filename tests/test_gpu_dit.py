@@ -1,7 +1,7 @@
 """The DiT denoise step (config 4) on the GPU against the CPU oracle of the same block math (oracle/dit_oracle.py):
 seeded random-init weights of the architecture, latents N(0,1) [image, 64], text states N(0,1).
 
-Bar: the seeded latent after one Euler step reaches cosine >= 0.999 against the oracle; the
+Bar (the north-star parity bar): the seeded latent after one Euler step reaches cosine >= 0.999 against the oracle; the
 test holds the stricter velocity (the transformer output) to the same cosine, and max-rel <= 5e-2 (every stored
 activation is rounded to bf16 / bfp16 on both sides, and a rounding tie that goes the other way moves one value by one
 bfp16 step)."""

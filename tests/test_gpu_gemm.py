@@ -91,7 +91,7 @@ def test_linear_bf16_out_no_bias(env, variant):
 
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_linear_config1_full_size(env, variant):
-    """BASELINE config 1 (DiT FFN up-projection): X[4352, 3072] ~ N(0,1), W[3072, 12288] ~ N(0, 0.02), bias
+    """Benchmark config 1 (DiT FFN up-projection): X[4352, 3072] ~ N(0,1), W[3072, 12288] ~ N(0, 0.02), bias
     ~ N(0, 0.01), bf16 out. The oracle runs on a sample of 256 rows (every M tile, first and last rows)."""
     torch = env[0]
     x, W, b = _case(4352, 3072, 12288, seed=0)
