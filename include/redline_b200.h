@@ -169,6 +169,15 @@ int rl_ln_mod(const uint16_t* x, const void* branch, int branch_dtype, const uin
               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream);
 
 /*
+ * RMSNorm residual glue of the Qwen3-VL text encoder. Replaces the vlm-rms / vlm-rms16 artifacts
+ * (kernels/vlm/rms_mod.cc, run by redline/vlm_run.py:340-341) and is checked against vlm_run.rms_ref
+ * (vlm_run.py:68-71): x' = bf16(x + g * branch), y = x' / sqrt(mean(x'^2) + 1e-6) * sc, rounded to bfp16 blocks of
+ * 8. Arguments, parameter rows and outputs as rl_ln_mod (the reference's rms_params have g = 1).
+ */
+int rl_rms_mod(const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
+               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream);
+
+/*
  * a11 - QK-RMSNorm + RoPE. Replaces the qkv_post artifact (kernels/glue/qkv_post.cc:112-178, run by forward.py:246)
  * and run_glue.rms_rope (redline/run_glue.py:27-37): per token and head, q and k are RMS-normalised over their 128
  * dims (eps 1e-6), scaled by w_q / w_k, and rotated on adjacent pairs (2i, 2i+1) by the token's (cos, sin).
@@ -179,6 +188,14 @@ int rl_ln_mod(const uint16_t* x, const void* branch, int branch_dtype, const uin
  */
 int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
                 uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream);
+
+/*
+ * rl_qkv_post for grouped-query attention: qkv (M, (H + 2 Hkv) * 128) = [q H heads | k Hkv heads | v Hkv heads]
+ * (the Qwen3-VL layer, redline/vlm_run.py:407-412, kernels/vlm/qkv_gqa_design.py). Out: q (H, M, 128), k (Hkv, M,
+ * 128), vt (Hkv, 128, ldv). rl_qkv_post(..., H, ...) is this with Hkv = H.
+ */
+int rl_qkv_post_gqa(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
+                    int Hkv, uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream);
 
 /*
  * a12 - joint text+image flash attention, head_dim 128, on tcgen05. Replaces the attention artifacts
@@ -193,6 +210,15 @@ int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, con
 int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int64_t Nq,
                  int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, int64_t ldo,
                  rl_stream_t stream);
+
+/*
+ * Grouped-query attention (the Qwen3-VL causal attention, kernels/vlm/attn_causal.cc, checked in the reference by
+ * vlm_run.attn_ref, vlm_run.py:181-190): H query heads over Hkv K/V heads, query head h reads K/V head
+ * h / (H / Hkv); k (Hkv, Nk, 128), vt (Hkv, 128, ldv); causal = row_limit[r] = r. rl_attention is this with Hkv = H.
+ */
+int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
+                     int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
+                     int64_t ldo, rl_stream_t stream);
 
 /* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from

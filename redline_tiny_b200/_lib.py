@@ -38,6 +38,9 @@ SIGNATURES = {
     "rl_swiglu_mlp_noalloc": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P]),
     "rl_ln_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "rl_qkv_post": (_I, [_P, _P, _P, _P, _I64, _I, _P, _P, _P, _I64, _P]),
+    "rl_qkv_post_gqa": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _I64, _P]),
+    "rl_rms_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
+    "rl_attention_gqa": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),
     "rl_swiglu_mlp": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P]),
 }
 

@@ -64,6 +64,7 @@ static_assert(sizeof(Barriers) <= 256, "barrier block");
 struct Params {
   int64_t Nq, Nk, nkv;
   int H;
+  int kv_group;               // query heads per K/V head (grouped-query attention; 1 = one K/V head per query head)
   const int32_t* row_limit;   // per query row: last visible key (inclusive), or null
   float scale_log2;           // logits = (q . k) * scale_log2, in log2 units (> 0)
   uint16_t* o;
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y;
+  const int kvh = h / p.kv_group;   // the K/V head this query head reads
   const int nblk = p.nblk;
 
   if (threadIdx.x == 0) {
@@ -171,8 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&bars->k_empty[s], ph ^ 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->k_full[s], K_BYTES);
           uint8_t* kt = smem + kK + s * K_BYTES;
-          tma_load_3d(kt, &tm_k, &bars->k_full[s], 0, t * BKV, h);
-          tma_load_3d(kt + K_SUB, &tm_k, &bars->k_full[s], 64, t * BKV, h);
+          tma_load_3d(kt, &tm_k, &bars->k_full[s], 0, t * BKV, kvh);
+          tma_load_3d(kt + K_SUB, &tm_k, &bars->k_full[s], 64, t * BKV, kvh);
           kf.note(s, ph);
         }
         if (t >= 1) {
@@ -181,8 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&bars->v_empty[s], ph ^ 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->v_full[s], V_BYTES);
           uint8_t* vt = smem + kV + s * V_BYTES;
-          tma_load_3d(vt, &tm_v, &bars->v_full[s], j * BKV, 0, h);
-          tma_load_3d(vt + V_SUB, &tm_v, &bars->v_full[s], j * BKV + 64, 0, h);
+          tma_load_3d(vt, &tm_v, &bars->v_full[s], j * BKV, 0, kvh);
+          tma_load_3d(vt + V_SUB, &tm_v, &bars->v_full[s], j * BKV + 64, 0, kvh);
           vf.note(s, ph);
         }
       }
@@ -391,14 +393,15 @@ inline int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 
 extern "C" {
 
-int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int64_t Nq,
-                 int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, int64_t ldo,
-                 rl_stream_t stream) {
+int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
+                     int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
+                     int64_t ldo, rl_stream_t stream) {
   using namespace rl;
   using namespace rl::attn;
   RL_REQUIRE(q && k && vt && o, RL_ERR_ARGUMENT, "rl_attention: NULL pointer");
   RL_REQUIRE(H > 0 && Nq >= 0 && Nk > 0 && nkv >= 0 && nkv <= Nk && ldv >= Nk && ldv % 8 == 0, RL_ERR_ARGUMENT,
              "rl_attention: need 0 <= nkv <= Nk <= ldv, ldv %% 8 == 0");
+  RL_REQUIRE(Hkv > 0 && H % Hkv == 0, RL_ERR_ARGUMENT, "rl_attention: %d query heads over %d K/V heads", H, Hkv);
   RL_REQUIRE(ldo >= static_cast<int64_t>(H) * HD && ldo % 8 == 0, RL_ERR_ARGUMENT,
              "rl_attention: ldo must be >= H * 128 and a multiple of 8");
   RL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(vt, 16) && aligned(o, 16) && aligned(row_limit, 4),
@@ -408,13 +411,14 @@ int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64
   CUtensorMap mq, mk, mv;
   int st;
   if ((st = make_map(&mq, q, HD, Nq, H, HD * 2, Nq * HD * 2, 64, BQ)) != RL_OK) return st;
-  if ((st = make_map(&mk, k, HD, Nk, H, HD * 2, Nk * HD * 2, 64, BKV)) != RL_OK) return st;
-  if ((st = make_map(&mv, vt, ldv, HD, H, ldv * 2, ldv * HD * 2, 64, HD)) != RL_OK) return st;
+  if ((st = make_map(&mk, k, HD, Nk, Hkv, HD * 2, Nk * HD * 2, 64, BKV)) != RL_OK) return st;
+  if ((st = make_map(&mv, vt, ldv, HD, Hkv, ldv * 2, ldv * HD * 2, 64, HD)) != RL_OK) return st;
   Params p;
   p.Nq = Nq;
   p.Nk = Nk;
   p.nkv = nkv;
   p.H = H;
+  p.kv_group = H / Hkv;
   p.row_limit = row_limit;
   p.scale_log2 = scale_log2;
   p.o = o;
@@ -429,6 +433,12 @@ int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64
   attention_kernel<<<grid, kThreads, kBytes, stream>>>(mq, mk, mv, p);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
+}
+
+int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int64_t Nq,
+                 int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, int64_t ldo,
+                 rl_stream_t stream) {
+  return rl_attention_gqa(q, k, vt, ldv, H, H, Nq, Nk, nkv, row_limit, scale_log2, o, ldo, stream);
 }
 
 }  // extern "C"

@@ -57,8 +57,9 @@ __device__ __forceinline__ void load_branch(const void* br, int br_f32, int64_t 
 __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __restrict__ x,
                                                           const void* __restrict__ br, int br_f32,
                                                           const uint16_t* __restrict__ params, int64_t M, int64_t D,
-                                                          int64_t row_split, float eps, uint16_t* __restrict__ xo,
-                                                          uint16_t* __restrict__ y_dq, uint8_t* __restrict__ y_q) {
+                                                          int64_t row_split, float eps, int rms,
+                                                          uint16_t* __restrict__ xo, uint16_t* __restrict__ y_dq,
+                                                          uint8_t* __restrict__ y_q) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t KB = D >> 3;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < M; r += static_cast<int64_t>(gridDim.x) * kWarps) {
@@ -87,8 +88,9 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
     }
     s1 = warp_sum(s1);
     s2 = warp_sum(s2);
-    const float mean = s1 / static_cast<float>(D);
-    const float var = fmaxf(s2 / static_cast<float>(D) - mean * mean, 0.0f);
+    // LayerNorm, or RMSNorm (rms: no mean subtraction, the mean square as the variance)
+    const float mean = rms ? 0.0f : s1 / static_cast<float>(D);
+    const float var = rms ? s2 / static_cast<float>(D) : fmaxf(s2 / static_cast<float>(D) - mean * mean, 0.0f);
     const float rstd = 1.0f / sqrtf(var + eps);
     // pass 2: y = (x' - mean) * rstd * sc, rounded to bfp16 blocks of 8 along the row; x' is read back from xo
     // when the caller asked for it (each lane reads the blocks it wrote itself in pass 1)
@@ -141,13 +143,14 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16
                                                                     const float* __restrict__ cs,
                                                                     const float* __restrict__ wq,
                                                                     const float* __restrict__ wk, int64_t M, int H,
-                                                                    float eps, uint16_t* __restrict__ q,
+                                                                    int Hkv, float eps, uint16_t* __restrict__ q,
                                                                     uint16_t* __restrict__ k) {
   // one warp per token; a half-warp per head (lane & 15 = 16-byte chunk of 8 dims = 4 RoPE pairs), so each step
   // covers two heads with fully coalesced 256-byte loads and a 16-lane (4-level) sum of squares
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hh = lane >> 4, c = lane & 15;
-  const int64_t ld = static_cast<int64_t>(3) * H * 128;
+  const int64_t ld = static_cast<int64_t>(H + 2 * Hkv) * 128;   // [q H heads | k Hkv heads | v Hkv heads]
+  const int nh = H + Hkv;                                           // normalised heads per token
   const float4 wq0 = __ldg(reinterpret_cast<const float4*>(wq) + 2 * c), wq1 = __ldg(reinterpret_cast<const float4*>(wq) + 2 * c + 1);
   const float4 wk0 = __ldg(reinterpret_cast<const float4*>(wk) + 2 * c), wk1 = __ldg(reinterpret_cast<const float4*>(wk) + 2 * c + 1);
   for (int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + warp; m < M; m += static_cast<int64_t>(gridDim.x) * kWarps) {
@@ -155,8 +158,10 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16
     const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + m * 128) + 2 * c + 1);  // pairs 4c+2, 4c+3
     const uint16_t* row = qkv + m * ld;
 #pragma unroll 4
-    for (int i = 0; i < H; ++i) {                     // heads u = 2i + hh: u < H is q head u, else k head u - H
-      const int u = 2 * i + hh;
+    for (int i = 0; i < (nh + 1) / 2; ++i) {          // heads u = 2i + hh: u < H is q head u, else k head u - H
+      const int u0 = 2 * i + hh;
+      const bool valid = u0 < nh;                     // an odd head count leaves the last half-warp idle
+      const int u = valid ? u0 : nh - 1;
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row + static_cast<int64_t>(u) * 128) + c);
       float v[8];
       const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16
         out[j] = pack_bf16x2_rn(n0 * co - n1 * si, n0 * si + n1 * co);
       }
       uint16_t* dst = isq ? q + (static_cast<int64_t>(u) * M + m) * 128 : k + (static_cast<int64_t>(u - H) * M + m) * 128;
-      reinterpret_cast<uint4*>(dst)[c] = make_uint4(out[0], out[1], out[2], out[3]);
+      if (valid) reinterpret_cast<uint4*>(dst)[c] = make_uint4(out[0], out[1], out[2], out[3]);
     }
   }
 }
@@ -193,9 +198,9 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_tok_kernel(const uint16
 // transposing 2-byte stores (16 dim groups per warp) spread over 8 bank groups and the row reads stay 16-byte
 // vectors.
 __global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t* __restrict__ qkv, int64_t M, int H,
-                                                                 int64_t ldv, uint16_t* __restrict__ vt) {
+                                                                 int Hkv, int64_t ldv, uint16_t* __restrict__ vt) {
   __shared__ __align__(16) uint16_t tile[128 * 64];
-  const int64_t ld = static_cast<int64_t>(3) * H * 128;
+  const int64_t ld = static_cast<int64_t>(H + 2 * Hkv) * 128;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64;
   const int h = blockIdx.y;
   auto at = [](int d, int t) { return d * 64 + ((((t >> 3) ^ (d >> 3)) & 7) << 3) + (t & 7); };
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) v_transpose16_kernel(const uint16_t*
     const int t = cid >> 4, dg = cid & 15;
     const int64_t m = m0 + t;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (m < M) v = __ldg(reinterpret_cast<const uint4*>(qkv + m * ld + (static_cast<int64_t>(2) * H + h) * 128) + dg);
+    if (m < M) v = __ldg(reinterpret_cast<const uint4*>(qkv + m * ld + (static_cast<int64_t>(H) + Hkv + h) * 128) + dg);
     const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -234,29 +239,40 @@ inline int grid_rows(int64_t units, int per_cta) {
 }  // namespace glue
 }  // namespace rl
 
+namespace rl {
+static int norm_mod(const char* fn, int rms, const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
+                    int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream) {
+  RL_REQUIRE(x && params, RL_ERR_ARGUMENT, "%s: NULL pointer", fn);
+  RL_REQUIRE(M >= 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT, "%s: need D %% 8 == 0", fn);
+  RL_REQUIRE(branch_dtype == RL_BF16 || branch_dtype == RL_F32, RL_ERR_ARGUMENT, "%s: bad branch dtype", fn);
+  RL_REQUIRE(aligned(x, 16) && aligned(branch, 16) && aligned(params, 16) && aligned(x_out, 16) && aligned(y_dq, 16),
+             RL_ERR_ALIGNMENT, "%s: bf16 pointers must be 16-byte aligned", fn);
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "%s: needs an sm_100 device", fn);
+  if (M == 0) return RL_OK;
+  glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
+      x, branch, branch_dtype == RL_F32 ? 1 : 0, params, M, D, row_split, 1e-6f, rms, x_out, y_dq, y_q);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+}  // namespace rl
+
 extern "C" {
 
 int rl_ln_mod(const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream) {
-  using namespace rl;
-  RL_REQUIRE(x && params, RL_ERR_ARGUMENT, "rl_ln_mod: NULL pointer");
-  RL_REQUIRE(M >= 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT, "rl_ln_mod: need D %% 8 == 0");
-  RL_REQUIRE(branch_dtype == RL_BF16 || branch_dtype == RL_F32, RL_ERR_ARGUMENT, "rl_ln_mod: bad branch dtype");
-  RL_REQUIRE(aligned(x, 16) && aligned(branch, 16) && aligned(params, 16) && aligned(x_out, 16) && aligned(y_dq, 16),
-             RL_ERR_ALIGNMENT, "rl_ln_mod: bf16 pointers must be 16-byte aligned");
-  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod: needs an sm_100 device");
-  if (M == 0) return RL_OK;
-  glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      x, branch, branch_dtype == RL_F32 ? 1 : 0, params, M, D, row_split, 1e-6f, x_out, y_dq, y_q);
-  RL_TRY_CUDA(cudaGetLastError());
-  return RL_OK;
+  return rl::norm_mod("rl_ln_mod", 0, x, branch, branch_dtype, params, M, D, row_split, x_out, y_dq, y_q, stream);
 }
 
-int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
-                uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream) {
+int rl_rms_mod(const uint16_t* x, const void* branch, int branch_dtype, const uint16_t* params, int64_t M, int64_t D,
+               int64_t row_split, uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream) {
+  return rl::norm_mod("rl_rms_mod", 1, x, branch, branch_dtype, params, M, D, row_split, x_out, y_dq, y_q, stream);
+}
+
+int rl_qkv_post_gqa(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
+                    int Hkv, uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream) {
   using namespace rl;
   RL_REQUIRE(qkv && rope_cs && w_q && w_k && q && k && vt, RL_ERR_ARGUMENT, "rl_qkv_post: NULL pointer");
-  RL_REQUIRE(M >= 0 && H > 0 && ldv >= M && ldv % 8 == 0, RL_ERR_ARGUMENT,
+  RL_REQUIRE(M >= 0 && H > 0 && Hkv > 0 && ldv >= M && ldv % 8 == 0, RL_ERR_ARGUMENT,
              "rl_qkv_post: need ldv >= M and ldv %% 8 == 0");
   RL_REQUIRE(aligned(qkv, 16) && aligned(rope_cs, 16) && aligned(w_q, 16) && aligned(w_k, 16) && aligned(q, 16) &&
                  aligned(k, 16) && aligned(vt, 16),
@@ -264,12 +280,17 @@ int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, con
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_qkv_post: needs an sm_100 device");
   if (M == 0) return RL_OK;
   glue::qk_norm_rope_tok_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      qkv, rope_cs, w_q, w_k, M, H, 1e-6f, q, k);
+      qkv, rope_cs, w_q, w_k, M, H, Hkv, 1e-6f, q, k);
   RL_TRY_CUDA(cudaGetLastError());
-  const dim3 grid(static_cast<unsigned>((ldv + 63) / 64), static_cast<unsigned>(H));
-  glue::v_transpose16_kernel<<<grid, glue::kThreads, 0, stream>>>(qkv, M, H, ldv, vt);
+  const dim3 grid(static_cast<unsigned>((ldv + 63) / 64), static_cast<unsigned>(Hkv));
+  glue::v_transpose16_kernel<<<grid, glue::kThreads, 0, stream>>>(qkv, M, H, Hkv, ldv, vt);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
+}
+
+int rl_qkv_post(const uint16_t* qkv, const float* rope_cs, const float* w_q, const float* w_k, int64_t M, int H,
+                uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream) {
+  return rl_qkv_post_gqa(qkv, rope_cs, w_q, w_k, M, H, H, q, k, vt, ldv, stream);
 }
 
 }  // extern "C"

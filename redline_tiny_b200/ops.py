@@ -163,9 +163,9 @@ def swiglu_mlp(x, w_up, w_down, out=None, out_dtype=torch.bfloat16, x_quantized=
     return out
 
 
-def ln_mod(x, branch, params, row_split=0, want_x=True, want_y_bytes=False):
-    """x' = bf16(x + g * branch); y = LayerNorm(x') * sc rounded to bfp16 (run_ln.ln_ref).
-    params: bf16 (2, 2, D) = two rows [g | sc] (run_ln.ln_params); rows < row_split use row 1.
+def ln_mod(x, branch, params, row_split=0, want_x=True, want_y_bytes=False, rms=False):
+    """x' = bf16(x + g * branch); y = LayerNorm(x') * sc (rms=True: RMSNorm, vlm_run.rms_ref) rounded to bfp16
+    (run_ln.ln_ref). params: bf16 (2, 2, D) = two rows [g | sc] (run_ln.ln_params); rows < row_split use row 1.
     Returns (x' bf16 or None, y decoded bf16, y bfp16 bytes or None)."""
     _check_cuda(x, branch, params)
     M, D = x.shape
@@ -173,27 +173,30 @@ def ln_mod(x, branch, params, row_split=0, want_x=True, want_y_bytes=False):
     y = torch.empty_like(x)
     yq = torch.empty(M * D // 8 * 9, dtype=torch.uint8, device=x.device) if want_y_bytes else None
     bdt = L.RL_BF16 if branch is None else _dtype_code(branch)
-    L.call("rl_ln_mod", _ptr(x), _ptr(branch), bdt, _ptr(params), M, D, int(row_split), _ptr(xo), _ptr(y), _ptr(yq),
-           _stream())
+    L.call("rl_rms_mod" if rms else "rl_ln_mod", _ptr(x), _ptr(branch), bdt, _ptr(params), M, D, int(row_split),
+           _ptr(xo), _ptr(y), _ptr(yq), _stream())
     return xo, y, yq
 
 
-def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None):
-    """QKV GEMM output (M, 3*H*128) -> q, k (H, M, 128) after RMSNorm * w and RoPE; vt (H, 128, ldv) = V^T."""
+def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
+    """QKV GEMM output (M, (H + 2 Hkv) * 128) -> q (H, M, 128), k (Hkv, M, 128) after RMSNorm * w and RoPE;
+    vt (Hkv, 128, ldv) = V^T. kv_heads defaults to heads (no grouping)."""
     _check_cuda(qkv, rope_cs, w_q, w_k)
     M = qkv.shape[0]
+    hkv = heads if kv_heads is None else int(kv_heads)
     ldv = ldv or (M + 127) // 128 * 128
     q = torch.empty((heads, M, 128), dtype=torch.bfloat16, device=qkv.device)
-    k = torch.empty_like(q)
-    vt = torch.empty((heads, 128, ldv), dtype=torch.bfloat16, device=qkv.device)
-    L.call("rl_qkv_post", _ptr(qkv), _ptr(rope_cs), _ptr(w_q), _ptr(w_k), M, heads, _ptr(q), _ptr(k), _ptr(vt), ldv,
-           _stream())
+    k = torch.empty((hkv, M, 128), dtype=torch.bfloat16, device=qkv.device)
+    vt = torch.empty((hkv, 128, ldv), dtype=torch.bfloat16, device=qkv.device)
+    L.call("rl_qkv_post_gqa", _ptr(qkv), _ptr(rope_cs), _ptr(w_q), _ptr(w_k), M, heads, hkv, _ptr(q), _ptr(k),
+           _ptr(vt), ldv, _stream())
     return q, k, vt
 
 
 def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo=None):
-    """Flash attention per head: q (H, Nq, 128), k (H, Nk, 128), vt (H, 128, ldv) bf16 -> o (Nq, ldo) bf16 with
-    head h at columns 128h.. (rounded to bfp16 along the head dim). scale_log2 defaults to log2(e)/sqrt(128)."""
+    """Flash attention per head: q (H, Nq, 128), k (Hkv, Nk, 128), vt (Hkv, 128, ldv) bf16 -> o (Nq, ldo) bf16 with
+    head h at columns 128h.. (rounded to bfp16 along the head dim); with Hkv < H query head h reads K/V head
+    h / (H / Hkv) (grouped-query attention). scale_log2 defaults to log2(e)/sqrt(128)."""
     import math
     _check_cuda(q, k, vt, row_limit, out)
     H, Nq, _ = q.shape
@@ -206,8 +209,8 @@ def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo
         out = torch.empty((Nq, ldo), dtype=torch.bfloat16, device=q.device)
     if row_limit is not None and row_limit.dtype != torch.int32:
         raise ValueError("row_limit must be int32")
-    L.call("rl_attention", _ptr(q), _ptr(k), _ptr(vt), ldv, H, Nq, Nk, nkv, _ptr(row_limit), scale_log2, _ptr(out),
-           ldo, _stream())
+    L.call("rl_attention_gqa", _ptr(q), _ptr(k), _ptr(vt), ldv, H, k.shape[0], Nq, Nk, nkv, _ptr(row_limit),
+           scale_log2, _ptr(out), ldo, _stream())
     return out
 
 
