@@ -220,6 +220,20 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
                      int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
                      int64_t ldo, rl_stream_t stream);
 
+/*
+ * VAE decoder convolution, 3x3 pad 1 (taps = 3) or 1x1 (taps = 1), stride 1, with bfp16 weights. Replaces the vconv
+ * artifacts (kernels/vae/vconv.cc:1-17, redline/vae_decode.py:168-194; weights packed by vae_ops.pack_vconv,
+ * vae_ops.py:44-61) and is checked against vae_ops.conv_ref (vae_ops.py:64-75).
+ * x: (H, W, Cin) bf16 holding bfp16-exact values (rl_quantize_bfp16's decoded output of the (H * W, Cin) matrix);
+ * w_native: the native tiles of B = [(dy * taps + dx) * Cin + ci][co] = w[co][ci][dy][dx] (K = taps^2 * Cin, a
+ * multiple of 64; N = Cout, a multiple of 128 - pad smaller outputs); bias: bf16 [Cout] or NULL; out: (H, W, Cout)
+ * bf16. workspace: rl_conv2d_workspace(H, W, Cin, taps) bytes (the im2col rows of the 3x3 conv; 0 for 1x1).
+ */
+size_t rl_conv2d_workspace(int H, int W, int Cin, int taps);
+int rl_conv2d_bfp16(const uint16_t* x, int H, int W, int Cin, const uint8_t* w_native, int Cout, int taps,
+                    const uint16_t* bias, uint16_t* out, void* workspace, size_t workspace_bytes,
+                    rl_stream_t stream);
+
 /* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
  * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel

@@ -5,3 +5,4 @@
 #include "rl_gemm.cu"
 #include "rl_glue.cu"
 #include "rl_attn.cu"
+#include "rl_conv.cu"

@@ -214,6 +214,34 @@ def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo
     return out
 
 
+def conv_weight(w, bias=None, cout_pad=128):
+    """Conv weight (Cout, Cin, k, k), k = 3 or 1, on the GPU -> (PackedWeight of B = [(dy, dx, ci)][co], bf16 bias or
+    None, taps). Cout is zero-padded to a multiple of `cout_pad` (the GEMM's N tile)."""
+    _check_cuda(w, bias)
+    cout, cin, k, _ = w.shape
+    n = (cout + cout_pad - 1) // cout_pad * cout_pad
+    B = torch.zeros((k * k * cin, n), dtype=torch.float32, device=w.device)
+    B[:, :cout] = w.float().permute(2, 3, 1, 0).reshape(k * k * cin, cout)
+    b = None
+    if bias is not None:
+        b = torch.zeros(n, dtype=torch.bfloat16, device=w.device)
+        b[:cout] = bias.to(torch.bfloat16)
+    return PackedWeight.from_float(B), b, k
+
+
+def conv2d(x_dq, w, bias, taps, out=None):
+    """VAE conv: x_dq (H, W, Cin) bf16 holding bfp16 values -> (H, W, N) bf16 (N = the padded Cout)."""
+    _check_cuda(x_dq, w.native, bias, out)
+    H, Wd, C = x_dq.shape
+    if out is None:
+        out = torch.empty((H, Wd, w.N), dtype=torch.bfloat16, device=x_dq.device)
+    nbytes = L.lib().rl_conv2d_workspace(H, Wd, C, taps)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x_dq.device)
+    L.call("rl_conv2d_bfp16", _ptr(x_dq), H, Wd, C, _ptr(w.native), w.N, taps, _ptr(bias), _ptr(out), _ptr(ws),
+           ws.numel(), _stream())
+    return out
+
+
 def set_gemm_variant(v):
     return L.lib().rl_set_gemm_variant(int(v))
 

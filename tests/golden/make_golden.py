@@ -200,6 +200,18 @@ def main(ref_root):
     out["normout_05"] = hg.norm_out_scale(hw, te)
     out["model_t"] = np.array([fw.model_t(s) for s in fw.SIGMAS])
 
+    # --- VAE decoder conv (vae_ops.py:44-75): the weight stream of pack_vconv and conv_ref, own seeded generator
+    sys.path.insert(0, str(Path(ref_root) / "kernels" / "vae"))
+    import vae_ops as vo
+    rv = np.random.default_rng(11)
+    wv = (rv.standard_normal((32, 16, 3, 3)) * 0.05).astype(np.float32)
+    bv = (rv.standard_normal(32) * 0.01).astype(np.float32)
+    xv = rv.standard_normal((6, 7, 16)).astype(np.float32)
+    out["vconv_w"], out["vconv_b"], out["vconv_x"] = wv, bv, xv
+    out["vconv_packed"] = vo.pack_vconv(wv, bv, 16, 16)
+    out["vconv_ref"] = vo.conv_ref(xv, wv, bv)
+    out["vconv1_ref"] = vo.conv_ref(xv, wv[:, :, 1:2, 1:2], bv)
+
     dst = Path(__file__).with_name("golden.npz")
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size / 1e3:.0f} KB, {len(out)} arrays)")

@@ -1,0 +1,48 @@
+"""GPU parity of the VAE decoder convolution (rl_conv2d_bfp16: im2col + the packed-weight GEMM) against the CPU
+oracle (oracle/vae_oracle.conv_ref = vae_ops.conv_ref on the bfp16-rounded activations and weights the reference's
+vconv multiplies). Output is bf16: max-rel <= 2e-3 + 2^-8 (the GEMM bar plus the output's own bf16 rounding)."""
+
+import numpy as np
+import pytest
+
+from oracle import bfp16_oracle as O
+from oracle import vae_oracle as VO
+
+pytestmark = pytest.mark.gpu
+
+BF16_OUT_TOL = 2e-3 + 2.0 ** -8
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    from redline_tiny_b200 import ops
+    assert torch.cuda.is_available()
+    return torch, ops, torch.device("cuda:0")
+
+
+@pytest.mark.parametrize("H,W,Cin,Cout,k", [(24, 20, 64, 128, 3), (24, 20, 64, 128, 1), (17, 9, 128, 3, 3),
+                                            (64, 64, 128, 256, 3), (32, 32, 512, 512, 1)])
+def test_conv2d(env, H, W, Cin, Cout, k):
+    torch, ops, dev = env
+    rng = np.random.default_rng(H * W + Cin + k)
+    x = rng.standard_normal((H, W, Cin)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, k, k)) * 0.05).astype(np.float32)
+    b = O.bf16_round((rng.standard_normal(Cout) * 0.01).astype(np.float32))
+    _, xq = ops.quantize_bfp16(torch.from_numpy(x.reshape(H * W, Cin)).to(dev))
+    pw, bias, taps = ops.conv_weight(torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    y = ops.conv2d(xq.view(H, W, Cin), pw, bias, taps)
+    ops.device_status()
+    got = y.float().cpu().numpy()[:, :, :Cout]
+    ref = VO.conv_ref(VO.quantize_pixels(x), VO.decode_conv_b(w), b)
+    err = O.max_rel(got, ref)
+    assert err <= BF16_OUT_TOL, f"max-rel {err:.3e}"
+
+
+def test_conv2d_rejects_bad_shapes(env):
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    x = torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev)
+    pw, _, _ = ops.conv_weight(torch.zeros((128, 64, 3, 3), device=dev))
+    with pytest.raises(L.RedlineError):
+        ops.conv2d(x, pw, None, 3)          # Cin = 12: 9 * 12 is not a multiple of 64

@@ -130,3 +130,14 @@ def test_host_glue_temb_modulation(golden):
     assert np.array_equal(HG.modulation(w, te), golden["mod_05"])
     assert np.array_equal(HG.norm_out_scale(w, te), golden["normout_05"])
     assert np.array_equal(np.array([HG.model_t(s) for s in HG.SIGMAS]), golden["model_t"])
+
+
+def test_vae_conv_oracle_and_weight_blocks(golden):
+    """The VAE conv oracle reproduces vae_ops.conv_ref (3x3 and 1x1), and the B200 conv's weight rounding (pack_b
+    blocks of B = [(dy, dx, ci)][co]) gives exactly the values of the reference's pack_vconv stream."""
+    from oracle import vae_oracle as VO
+    w, b, x = golden["vconv_w"], golden["vconv_b"], golden["vconv_x"]
+    assert np.allclose(VO.conv_ref(x, w, b), golden["vconv_ref"], rtol=0, atol=1e-12)
+    assert np.allclose(VO.conv_ref(x, w[:, :, 1:2, 1:2], b), golden["vconv1_ref"], rtol=0, atol=1e-12)
+    ref_w = VO.unpack_vconv_weights(golden["vconv_packed"], 32, 16, 3, 16, 16)
+    assert np.array_equal(VO.decode_conv_b(w), ref_w)
