@@ -233,6 +233,8 @@ def conv2d(x_dq, w, bias, taps, out=None):
     """VAE conv: x_dq (H, W, Cin) bf16 holding bfp16 values -> (H, W, N) bf16 (N = the padded Cout)."""
     _check_cuda(x_dq, w.native, bias, out)
     H, Wd, C = x_dq.shape
+    if w.K != taps * taps * C:
+        raise ValueError(f"conv weight has K = {w.K}, a {taps}x{taps} conv over {C} channels needs {taps * taps * C}")
     if out is None:
         out = torch.empty((H, Wd, w.N), dtype=torch.bfloat16, device=x_dq.device)
     nbytes = L.lib().rl_conv2d_workspace(H, Wd, C, taps)

@@ -42,7 +42,11 @@ def test_conv2d(env, H, W, Cin, Cout, k):
 def test_conv2d_rejects_bad_shapes(env):
     torch, ops, dev = env
     from redline_tiny_b200 import _lib as L
-    x = torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev)
     pw, _, _ = ops.conv_weight(torch.zeros((128, 64, 3, 3), device=dev))
-    with pytest.raises(L.RedlineError):
-        ops.conv2d(x, pw, None, 3)          # Cin = 12: 9 * 12 is not a multiple of 64
+    with pytest.raises(ValueError):         # weight packed for 64 input channels, input has 12
+        ops.conv2d(torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev), pw, None, 3)
+    x = torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(4 * 4 * 9 * 12 * 2, dtype=torch.uint8, device=dev)
+    with pytest.raises(L.RedlineError):     # the C ABI: 9 * 12 is not a multiple of 64
+        L.call("rl_conv2d_bfp16", x.data_ptr(), 4, 4, 12, pw.native.data_ptr(), 128, 3, None, x.data_ptr(),
+               ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
