@@ -241,6 +241,11 @@ int rl_conv2d_bfp16(const uint16_t* x, int H, int W, int Cin, const uint8_t* w_n
  * 1000*P + 100*G + 10*V + S also select the decode split and the pipeline depth. Returns the previous value. */
 int rl_set_gemm_variant(int variant);
 
+/* Attention kernel for tests and benchmarks: 0 = default (two 128-query tiles per CTA, the tensor pipe working on one
+ * tile while the other's softmax runs), 1 = one query tile per CTA, 2-5 = two-tile forms (2 + 2 * in-order Q.K issue
+ * + P released in two halves). Returns the previous value. */
+int rl_set_attention_variant(int variant);
+
 #ifdef __cplusplus
 }
 #endif

@@ -109,8 +109,8 @@ struct InFlight {
     issued |= 1u << s;
     parity = (parity & ~(1u << s)) | (ph << s);
   }
-  __device__ void drain(uint64_t* full) const {
-    for (int s = 0; s < kStages; ++s)
+  __device__ void drain(uint64_t* full, int stages = kStages) const {
+    for (int s = 0; s < stages; ++s)
       if (issued & (1u << s)) mbar_drain(&full[s], (parity >> s) & 1);
   }
 };
@@ -373,6 +373,388 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// One 128-key block of the online softmax for the calling thread's query row (thread = TMEM lane): S is read from
+// TMEM at `ta` (128 fp32 columns), masked past key `lim`, the running maximum raised lazily (by more than kTau), the
+// thread's O row at `to` rescaled when it rises and `o_live` (a previous P.V has accumulated into it), and
+// P = 2^(logit - m) written back over S as bf16 pairs, in two halves of 64 keys. The warp arrives on p_bar[0] once
+// P is stored (kSplitP: on p_bar[0] after the first half and p_bar[1] after the second, so the MMA of the first
+// half overlaps the exponentials of the second). Scaling and row sums use packed f32x2 arithmetic.
+template <bool kSplitP>
+__device__ __forceinline__ void softmax_block(uint32_t ta, uint32_t to, int64_t key0, int64_t lim, float scl,
+                                              bool o_live, float& m_run, float& l_run, uint64_t* p_bar, int lane) {
+  uint32_t s[BKV];
+#pragma unroll
+  for (int c = 0; c < BKV / 32; ++c) {
+    uint32_t (&sc)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]);
+    RL_TMEM_LD32(ta + 32 * c, sc);
+  }
+  tmem_ld_wait_regs(s);
+  if (key0 + BKV - 1 > lim) {
+#pragma unroll
+    for (int c = 0; c < BKV; ++c)
+      if (key0 + c > lim) s[c] = 0xFF800000u;  // -inf
+  }
+  float mx;
+  {
+    float m8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m8[i] = max3f(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]), -INFINITY);
+#pragma unroll
+    for (int c = 16; c < BKV; c += 16)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], __uint_as_float(s[c + 2 * i]), __uint_as_float(s[c + 2 * i + 1]));
+    mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+  }
+  mx *= scl;
+  const bool raise = mx > m_run + kTau;
+  float alpha = 1.0f;
+  if (raise) {
+    alpha = exp2f(m_run - mx);
+    l_run *= alpha;
+    m_run = mx;
+  }
+  const bool rescale = o_live && __any_sync(0xffffffffu, raise);
+  const bool none = m_run == -INFINITY;
+  const float2 sc2 = make_float2(scl, scl), nm2 = make_float2(-m_run, -m_run);
+  float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    uint32_t pk[32];
+    if (none) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) pk[c] = 0u;
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int i = 64 * hh + 2 * c;
+        const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])), sc2, nm2);
+        const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        acc[c & 3] = __fadd2_rn(acc[c & 3], e);
+        pk[c] = pack_bf16x2(e.x, e.y);
+      }
+    }
+    RL_TMEM_ST32(ta + 32 * hh, pk);
+    // rows whose running maximum rose rescale O (quiescent: the previous P.V completed before S was committed),
+    // after the first half's exponentials so that the scores of that half no longer hold registers
+    if (hh == 0 && rescale) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        RL_TMEM_LD32(to + 32 * c, o);
+        tmem_ld_wait_regs(o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        RL_TMEM_ST32(to + 32 * c, o);
+        tmem_st_wait_regs(o);
+      }
+    }
+    if (kSplitP || hh == 1) {
+      tmem_st_wait_regs(pk);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_bar[kSplitP ? hh : 0]);
+    }
+  }
+  const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
+  const float2 a = __fadd2_rn(a01, a23);
+  l_run += a.x + a.y;
+}
+
+// O / l of the thread's query row, rounded to bfp16 blocks of 8 along the head dim, stored row-major.
+__device__ __forceinline__ void store_o_row(uint32_t to, float l_run, uint16_t* orow, bool store) {
+  const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    RL_TMEM_LD32(to + 32 * c, o);
+    tmem_ld_wait_regs(o);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      uint32_t bits[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) bits[i] = __float_as_uint(__uint_as_float(o[8 * b + i]) * inv);
+      uint32_t E, lo, hi, w[4];
+      bfp16_quant_block_fast(bits, E, lo, hi, w);
+      if (store) reinterpret_cast<uint4*>(orow + 32 * c + 8 * b)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Two query tiles per CTA (256 queries of one head). The MMA warp interleaves the tiles - P_0 V, S_0 = Q_0 K,
+// P_1 V, S_1 = Q_1 K per key block - so the tensor pipe works on one tile while the other tile's softmax runs, and
+// each K / V block is loaded once for both tiles. TMEM: S_0 [0, 128), S_1 [128, 256), O_0 [256, 384),
+// O_1 [384, 512); P_t is written over S_t. S_t of the next block overwrites P_t, which P_t.V reads: kInOrder issues
+// that Q.K right after the P.V (the tensor pipe runs one thread's MMAs in issue order, so the P.V has read its
+// operand first), otherwise the Q.K waits for the P.V's completion.
+// Warpgroup 0 (producer, MMA issuer, two idle warps) gives registers to the two softmax warpgroups (setmaxnreg):
+// a softmax thread holds its 128 scores and 64 packed probabilities.
+namespace two {
+constexpr int kThreads = 384;
+constexpr int KS = 3;                 // K pipeline depth
+constexpr int VS = 2;                 // V pipeline depth
+constexpr int kRegsLaunch = 168;      // registers per thread the kernel is launched with (65536 / 384, rounded to 8)
+constexpr int kRegsLow = 80;          // warpgroup 0 after setmaxnreg.dec (the MMA issuer spills below 80)
+constexpr int kRegsHigh = 208;        // softmax warpgroups after setmaxnreg.inc (no spills at 208)
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads * kRegsLaunch, "register split above the launch's total");
+static_assert(kRegsLow + 2 * kRegsHigh <= 512, "register split above one SM sub-partition's file");
+constexpr int kQ = 0;                 // Q_0, Q_1
+constexpr int kK = 2 * Q_BYTES;
+constexpr int kV = kK + KS * K_BYTES;
+constexpr int kBar = kV + VS * V_BYTES;
+constexpr int kBytes = 1024 + kBar + 256;
+static_assert(kBytes <= 232448, "shared memory");
+
+struct Barriers {
+  uint64_t q_full;
+  uint64_t k_full[KS];
+  uint64_t k_empty[KS];
+  uint64_t v_full[VS];
+  uint64_t v_empty[VS];
+  uint64_t s_full[2];
+  uint64_t p_full[2][2];   // [tile][half of P]; only [t][0] without kSplitP
+  uint64_t pv_done[2];
+  uint64_t o_full;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(Barriers) <= 256, "barrier block");
+
+template <bool kInOrder, bool kSplitP>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kBar);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt2 = blockIdx.x, h = blockIdx.y;
+  const int kvh = h / p.kv_group;
+  const int nblk = p.nblk;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t][0], 4);
+      mbar_init(&bars->p_full[t][1], 4);
+      mbar_init(&bars->pv_done[t], 1);
+    }
+    mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsLow>();
+  if (warp == 0) {
+    // ---------------- producer: Q_0, Q_1, then K(t) and V(t - 1) in turn ----------------
+    if (lane == 0) {
+      bool ok = true;
+      InFlight kf, vf;
+      mbar_arrive_expect_tx(&bars->q_full, 2 * Q_BYTES);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_3d(smem + kQ + t * Q_BYTES, &tm_q, &bars->q_full, 0, (2 * qt2 + t) * BQ, h);
+        tma_load_3d(smem + kQ + t * Q_BYTES + Q_BYTES / 2, &tm_q, &bars->q_full, 64, (2 * qt2 + t) * BQ, h);
+      }
+      for (int t = 0; ok && t <= nblk; ++t) {
+        if (t < nblk) {
+          const int s = t % KS;
+          const uint32_t ph = (t / KS) & 1;
+          if (!mbar_wait(&bars->k_empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->k_full[s], K_BYTES);
+          uint8_t* kt = smem + kK + s * K_BYTES;
+          tma_load_3d(kt, &tm_k, &bars->k_full[s], 0, t * BKV, kvh);
+          tma_load_3d(kt + K_SUB, &tm_k, &bars->k_full[s], 64, t * BKV, kvh);
+          kf.note(s, ph);
+        }
+        if (t >= 1) {
+          const int j = t - 1, s = j % VS;
+          const uint32_t ph = (j / VS) & 1;
+          if (!mbar_wait(&bars->v_empty[s], ph ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->v_full[s], V_BYTES);
+          uint8_t* vt = smem + kV + s * V_BYTES;
+          tma_load_3d(vt, &tm_v, &bars->v_full[s], j * BKV, 0, kvh);
+          tma_load_3d(vt + V_SUB, &tm_v, &bars->v_full[s], j * BKV + 64, 0, kvh);
+          vf.note(s, ph);
+        }
+      }
+      if (!ok) {
+        mbar_drain(&bars->q_full, 0);
+        kf.drain(bars->k_full, KS);
+        vf.drain(bars->v_full, VS);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (warp-wide, elected lane issues) ----------------
+    constexpr uint32_t idesc_s = idesc_bf16(BQ, BKV);
+    constexpr uint32_t idesc_o = idesc_bf16(BQ, HD);
+    bool any = false;
+    const uint32_t qa0 = smem_u32(smem + kQ);
+    // S_t = Q_t K_j^T, once P_t of block j - 1 has been read by its P.V
+    auto qk = [&](int t, int j) -> bool {
+      const int s = j % KS;
+      if (!mbar_wait_warp(&bars->k_full[s], (j / KS) & 1, abort)) return false;
+      if (!kInOrder && j > 0 && !mbar_wait_warp(&bars->pv_done[t], (j - 1) & 1, abort)) return false;
+      tc_fence_after();
+      const uint32_t qa = qa0 + t * Q_BYTES;
+      const uint32_t kb = smem_u32(smem + kK + s * K_BYTES);
+      if (elect_one()) {
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint64_t adesc = sdesc_kmajor_sw128(qa + (k >> 2) * (Q_BYTES / 2)) + 2 * (k & 3);
+          const uint64_t bdesc = sdesc_kmajor_sw128(kb + (k >> 2) * K_SUB) + 2 * (k & 3);
+          umma_ss(tmem + t * BKV, adesc, bdesc, idesc_s, k ? 1u : 0u);
+        }
+        umma_commit(&bars->s_full[t]);
+        if (t == 1) umma_commit(&bars->k_empty[s]);
+      }
+      __syncwarp();
+      any = true;
+      return true;
+    };
+    // O_t += P_t V_j (kSplitP: the first 64 keys as soon as their half of P is stored)
+    auto pv = [&](int t, int j) -> bool {
+      const int s = j % VS;
+      if (!mbar_wait_warp(&bars->v_full[s], (j / VS) & 1, abort)) return false;
+      const uint32_t vb = smem_u32(smem + kV + s * V_BYTES);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        if (hh == 0 || kSplitP) {
+          if (!mbar_wait_warp(&bars->p_full[t][hh], j & 1, abort)) return false;
+          tc_fence_after();
+        }
+        if (elect_one()) {
+#pragma unroll
+          for (int k = 4 * hh; k < 4 * hh + 4; ++k) {
+            const uint64_t bdesc = sdesc_kmajor_sw128(vb + (k >> 2) * V_SUB) + 2 * (k & 3);
+            umma_ts(tmem + kOCol + t * HD, tmem + t * BKV + k * 8, bdesc, idesc_o, (j | k) ? 1u : 0u);
+          }
+          if (hh == 1) {
+            if (!kInOrder) umma_commit(&bars->pv_done[t]);
+            if (t == 1) umma_commit(&bars->v_empty[s]);
+          }
+        }
+        __syncwarp();
+      }
+      return true;
+    };
+    bool ok = mbar_wait_warp(&bars->q_full, 0, abort) && qk(0, 0) && qk(1, 0);
+    for (int j = 1; ok && j < nblk; ++j) ok = pv(0, j - 1) && qk(0, j) && pv(1, j - 1) && qk(1, j);
+    if (ok) ok = pv(0, nblk - 1) && pv(1, nblk - 1);
+    if (elect_one()) {
+      if (ok) umma_commit(&bars->o_full);
+      if (!ok && any) {
+        umma_commit(&bars->drain);
+        mbar_drain(&bars->drain, 0);
+      }
+    }
+    __syncwarp();
+  }
+  } else {
+    setmaxnreg_inc<kRegsHigh>();
+    // ---------------- softmax of query tile t (thread = query row = TMEM lane) ----------------
+    // S_t of block j is committed after P_t.V of block j - 1 was issued, so its arrival also means O_t is quiescent
+    // and may be rescaled.
+    const int t = (warp - 4) >> 2;
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    const int64_t qrow = (static_cast<int64_t>(qt2) * 2 + t) * BQ + row;
+    const uint32_t lane_off = (32u * q) << 16;
+    const uint32_t ta = tmem + t * BKV + lane_off;
+    const uint32_t to = tmem + kOCol + t * HD + lane_off;
+    int64_t lim = p.nkv - 1;
+    if (p.row_limit && qrow < p.Nq) lim = min(lim, static_cast<int64_t>(__ldg(p.row_limit + qrow)));
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      if (!mbar_wait(&bars->s_full[t], j & 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      softmax_block<kSplitP>(ta, to, static_cast<int64_t>(j) * BKV, lim, p.scale_log2, j > 0, m_run, l_run,
+                             bars->p_full[t], lane);
+    }
+    if (ok && nblk > 0 && mbar_wait(&bars->o_full, 0, abort)) {
+      tc_fence_after();
+      store_o_row(to, l_run, p.o + qrow * p.ldo + static_cast<int64_t>(h) * HD, qrow < p.Nq);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+}  // namespace two
+
+// Kernel choice for rl_attention_gqa: 0 = default (two query tiles per CTA, P released in halves, Q.K after the
+// P.V's completion: variant 3), 1 = one tile per CTA; 2-5 = the two-tile forms 2 + 2 * kInOrder + kSplitP. Measured
+// at config 3 (24 heads x 4352, B200): one tile 257 us, variant 2 221 us, 3 213 us, 4 215 us, 5 211 us - issuing
+// Q.K in order behind the P.V gains ~1 %, so the default keeps the explicit wait.
+inline int& variant() {
+  static int v = 0;
+  return v;
+}
+
+// The two-tile kernel raises its softmax warpgroups' registers with setmaxnreg.inc, which waits until warpgroup 0
+// has given enough back: that only ends if the kernel was compiled to launch with kRegsLaunch registers a thread.
+template <bool kInOrder, bool kSplitP>
+inline int two_tile_launch(dim3 grid, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                           const Params& p, cudaStream_t stream) {
+  auto kern = two::attention2_kernel<kInOrder, kSplitP>;
+  static int st = -1;
+  static int regs = 0;
+  if (st < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+      return fail(RL_ERR_CUDA, "rl_attention: cudaFuncGetAttributes failed");
+    regs = fa.numRegs;
+    if (regs != two::kRegsLaunch) {
+      st = RL_ERR_UNSUPPORTED;
+    } else if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, two::kBytes) != cudaSuccess) {
+      st = RL_ERR_CUDA;
+    } else {
+      st = RL_OK;
+    }
+  }
+  if (st != RL_OK)
+    return fail(st, "rl_attention: the two-tile kernel is unavailable (compiled with %d registers a thread, its "
+                "register split needs %d, and 227 KB of shared memory)", regs, two::kRegsLaunch);
+  kern<<<grid, two::kThreads, two::kBytes, stream>>>(mq, mk, mv, p);
+  return RL_OK;
+}
+
 inline int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                     uint64_t stride2, uint32_t b0, uint32_t b1) {
   EncodeTiledFn enc = encode_tiled();
@@ -428,11 +810,30 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
     RL_TRY_CUDA(cudaMemset2DAsync(o, ldo * 2, 0, static_cast<size_t>(H) * HD * 2, Nq, stream));
     return RL_OK;
   }
-  const dim3 grid(static_cast<unsigned>((Nq + BQ - 1) / BQ), static_cast<unsigned>(H));
-  RL_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes));
-  attention_kernel<<<grid, kThreads, kBytes, stream>>>(mq, mk, mv, p);
+  const int v = variant();
+  if (v != 1) {
+    const dim3 grid(static_cast<unsigned>((Nq + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(H));
+    switch (v) {
+      case 2: st = two_tile_launch<false, false>(grid, mq, mk, mv, p, stream); break;
+      case 3: st = two_tile_launch<false, true>(grid, mq, mk, mv, p, stream); break;
+      case 4: st = two_tile_launch<true, false>(grid, mq, mk, mv, p, stream); break;
+      case 5: st = two_tile_launch<true, true>(grid, mq, mk, mv, p, stream); break;
+      default: st = two_tile_launch<false, true>(grid, mq, mk, mv, p, stream); break;
+    }
+    if (st != RL_OK) return st;
+  } else {
+    const dim3 grid(static_cast<unsigned>((Nq + BQ - 1) / BQ), static_cast<unsigned>(H));
+    RL_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes));
+    attention_kernel<<<grid, kThreads, kBytes, stream>>>(mq, mk, mv, p);
+  }
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
+}
+
+int rl_set_attention_variant(int variant) {
+  const int prev = rl::attn::variant();
+  rl::attn::variant() = variant;
+  return prev;
 }
 
 int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int64_t Nq,

@@ -248,5 +248,10 @@ def set_gemm_variant(v):
     return L.lib().rl_set_gemm_variant(int(v))
 
 
+def set_attention_variant(v):
+    """0 = two query tiles per CTA (default), 1 = one query tile per CTA; returns the previous choice."""
+    return L.lib().rl_set_attention_variant(int(v))
+
+
 def device_status():
     return L.device_status()

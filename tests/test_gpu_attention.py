@@ -15,12 +15,16 @@ from oracle import bfp16_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def env():
+@pytest.fixture(scope="module", params=[0, 1, 2, 5], ids=["default", "one-tile", "two-tile-wait", "two-tile-inorder"])
+def env(request):
+    """The attention kernels: 0 = default (two query tiles per CTA, P in halves), 1 = one query tile per CTA,
+    2 = two tiles with P whole, 5 = two tiles with Q.K issued in order behind P.V."""
     import torch
     from redline_tiny_b200 import ops
     assert torch.cuda.is_available()
-    return torch, ops, torch.device("cuda:0")
+    prev = ops.set_attention_variant(request.param)
+    yield torch, ops, torch.device("cuda:0")
+    ops.set_attention_variant(prev)
 
 
 def _bf16(torch, a, dev):
