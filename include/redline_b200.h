@@ -234,6 +234,22 @@ int rl_conv2d_bfp16(const uint16_t* x, int H, int W, int Cin, const uint8_t* w_n
                     const uint16_t* bias, uint16_t* out, void* workspace, size_t workspace_bytes,
                     rl_stream_t stream);
 
+/* Per-step adaLN conditioning of the DiT (host_glue.py:31-48, forward.py:231-238), run on the GPU so the denoise
+ * step needs no host matrix work:
+ * rl_matvec_f32: y[r][n] = sum_k f(x[r][k]) w[n][k] (+ bias[n]) for r < R <= 4, f = SiLU when silu_in; w fp32
+ *   row-major (N, K), K % 4 == 0, R * K <= 12288; the linear_1 / linear_2 / modulation / norm_out products.
+ * rl_sinusoidal_embed: e (2, 2 * half) = [cos(t_r f_i) | sin(t_r f_i)] for rows t_0, t_1 (the timestep times 1000)
+ *   and frequencies f (half).
+ * rl_adaln_params: from mod (2, 4D) = [scale1 | gate1 | scale2 | gate2] and out_scale (2 rows of ld_out >= D; the
+ *   first D columns are used), the bf16 LayerNorm
+ *   parameter sets (2, 2, D) = rows [g | sc]: first (1, 1 + scale1), mlp (tanh gate1, 1 + scale2),
+ *   attn (tanh gate2, 1 + scale1), out (tanh gate2, 1 + out_scale). */
+int rl_matvec_f32(const float* w, int N, int K, const float* x, int R, const float* bias, int silu_in, float* y,
+                  rl_stream_t stream);
+int rl_sinusoidal_embed(float t0, float t1, const float* freqs, int half, float* e, rl_stream_t stream);
+int rl_adaln_params(const float* mod, const float* out_scale, int ld_out, int D, uint16_t* first, uint16_t* mlp,
+                    uint16_t* attn, uint16_t* out, rl_stream_t stream);
+
 /* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
  * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel

@@ -45,6 +45,9 @@ SIGNATURES = {
     "rl_rms_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "rl_attention_gqa": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),
     "rl_swiglu_mlp": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P]),
+    "rl_matvec_f32": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
+    "rl_sinusoidal_embed": (_I, [ctypes.c_float, ctypes.c_float, _P, _I, _P, _P]),
+    "rl_adaln_params": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
 }
 
 

@@ -6,3 +6,4 @@
 #include "rl_glue.cu"
 #include "rl_attn.cu"
 #include "rl_conv.cu"
+#include "rl_adaln.cu"

@@ -140,6 +140,29 @@ class DiT:
         self.img_in = pw(weights["img_in"])
         self.proj_out = pw(weights["proj_out"])
         self.host = weights["host"]
+        # adaLN conditioning weights, resident in fp32 for the per-step glue on the GPU (set_t)
+        te = "time_text_embed.timestep_embedder."
+
+        def f32(name, required=True):
+            a = self.host.get(name)
+            if a is None:
+                if required:
+                    raise KeyError(f"host weight {name} missing")
+                return None
+            return torch.as_tensor(np.asarray(a, np.float32)).to(dev).contiguous()
+        self.glue = {"l1w": f32(te + "linear_1.weight"), "l1b": f32(te + "linear_1.bias", False),
+                     "l2w": f32(te + "linear_2.weight"), "l2b": f32(te + "linear_2.bias", False),
+                     "mod": f32("modulation.1.weight"), "norm": f32("norm_out.linear.weight")}
+        self.freqs = torch.from_numpy(HG.timestep_freqs()).to(dev)
+        T = self.glue["l1w"].shape[0]
+        if (self.glue["l1w"].shape[1] != 2 * self.freqs.numel() or self.glue["mod"].shape != (4 * D, T)
+                or self.glue["norm"].shape[0] < D):
+            raise ValueError("adaLN weights do not match the config")
+        self.t_e = torch.empty(2, 2 * self.freqs.numel(), dtype=torch.float32, device=dev)
+        self.t_h = torch.empty(2, T, dtype=torch.float32, device=dev)
+        self.t_te = torch.empty(2, T, dtype=torch.float32, device=dev)
+        self.t_mod = torch.empty(2, 4 * D, dtype=torch.float32, device=dev)
+        self.t_out = torch.empty(2, self.glue["norm"].shape[0], dtype=torch.float32, device=dev)
         pad, shapes = HG.joint_layout(np.zeros(cfg.text, bool), n_target=cfg.image, grid=cfg.grid)
         self.rope_cs = torch.from_numpy(HG.rope(pad, shapes)).to(dev).contiguous()     # (M, 64, 2)
         bf = dict(dtype=torch.bfloat16, device=dev)
@@ -157,21 +180,29 @@ class DiT:
         self.h = torch.empty(M, F, **bf)
         self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
         self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
-        self.params = {}
+        self.params = {k: torch.empty(2, 2, D, **bf) for k in ("first", "mlp", "attn", "out")}
 
-    # --- host glue: per-step adaLN parameters (forward.py:231-238) ---
+    # --- per-step adaLN parameters (forward.py:231-238), computed on the GPU ---
     def set_t(self, sigma):
-        cfg, D = self.cfg, self.cfg.hidden
-        te = HG.temb(self.host, HG.model_t(sigma))
-        mod = HG.modulation(self.host, te)
-        out_scale = HG.norm_out_scale(self.host, te)
-        s1, g1, s2, g2 = (mod[:, i * D:(i + 1) * D] for i in range(4))
-
-        def lp(g, sc):
-            p = np.concatenate([np.asarray(g, np.float32), np.asarray(sc, np.float32)], 1).reshape(2, 2, D)
-            return torch.from_numpy(p).to(self.dev).to(torch.bfloat16).contiguous()
-        self.params = {"first": lp(np.ones((2, D)), 1 + s1), "mlp": lp(np.tanh(g1), 1 + s2),
-                       "attn": lp(np.tanh(g2), 1 + s1), "out": lp(np.tanh(g2), 1 + out_scale)}
+        """Timestep embedding -> modulation / norm_out -> the four bf16 LayerNorm parameter sets, as six small
+        kernels on the current stream (the reference runs these products on the host: host_glue.py:31-48)."""
+        D, g = self.cfg.hidden, self.glue
+        s = torch.cuda.current_stream().cuda_stream
+        T, half = self.t_h.shape[1], self.freqs.numel()
+        t0 = float(np.float32(HG.model_t(sigma)) * np.float32(1000.0))
+        ptr = lambda a: None if a is None else a.data_ptr()
+        L.call("rl_sinusoidal_embed", t0, 0.0, self.freqs.data_ptr(), half, self.t_e.data_ptr(), s)
+        L.call("rl_matvec_f32", g["l1w"].data_ptr(), T, 2 * half, self.t_e.data_ptr(), 2, ptr(g["l1b"]), 0,
+               self.t_h.data_ptr(), s)
+        L.call("rl_matvec_f32", g["l2w"].data_ptr(), T, T, self.t_h.data_ptr(), 2, ptr(g["l2b"]), 1,
+               self.t_te.data_ptr(), s)
+        L.call("rl_matvec_f32", g["mod"].data_ptr(), 4 * D, T, self.t_te.data_ptr(), 2, None, 1,
+               self.t_mod.data_ptr(), s)
+        L.call("rl_matvec_f32", g["norm"].data_ptr(), self.t_out.shape[1], T, self.t_te.data_ptr(), 2, None, 1,
+               self.t_out.data_ptr(), s)
+        L.call("rl_adaln_params", self.t_mod.data_ptr(), self.t_out.data_ptr(), self.t_out.shape[1], D,
+               self.params["first"].data_ptr(),
+               self.params["mlp"].data_ptr(), self.params["attn"].data_ptr(), self.params["out"].data_ptr(), s)
 
     def _linear(self, x, w, out, epi=L.RL_EPI_NONE, out_dtype=L.RL_BF16):
         M, K = x.shape

@@ -40,11 +40,15 @@ def _linear(x, w, b=None):
     return y + b if b is not None else y
 
 
+def timestep_freqs(half=128):
+    """The sinusoidal embedding's frequencies exp(-ln(10^4) i / half), float32 (host_glue.py:31-36)."""
+    return np.exp(-math.log(10000) * np.arange(half, dtype=np.float32) / half)
+
+
 def temb(w, t):
     """Sinusoidal(256) -> linear_1 -> SiLU -> linear_2 on rows [t, 0] (host_glue.py:31-40)."""
     ts = np.array([t, 0.0], np.float32) * 1000.0
-    half = 128
-    freqs = np.exp(-math.log(10000) * np.arange(half, dtype=np.float32) / half)
+    freqs = timestep_freqs()
     arg = ts[:, None] * freqs[None]
     e = np.concatenate([np.cos(arg), np.sin(arg)], -1).astype(np.float32)
     p = "time_text_embed.timestep_embedder."
@@ -60,6 +64,19 @@ def modulation(w, te):
 def norm_out_scale(w, te):
     """host_glue.py:47-48."""
     return _linear(silu(te), w["norm_out.linear.weight"])
+
+
+def adaln_params(mod, out_scale, D):
+    """The LayerNorm parameter sets of one step (forward.py:231-238), float32 (2, 2, D) = rows [g | sc] before their
+    bf16 rounding: first (1, 1 + scale1), mlp (tanh gate1, 1 + scale2), attn (tanh gate2, 1 + scale1),
+    out (tanh gate2, 1 + out_scale); mod = [scale1 | gate1 | scale2 | gate2]."""
+    s1, g1, s2, g2 = (np.asarray(mod[:, i * D:(i + 1) * D], np.float32) for i in range(4))
+    out_scale = np.asarray(out_scale[:, :D], np.float32)
+
+    def lp(g, sc):
+        return np.concatenate([np.asarray(g, np.float32), np.asarray(sc, np.float32)], 1).reshape(2, 2, D)
+    return {"first": lp(np.ones((2, D)), 1 + s1), "mlp": lp(np.tanh(g1), 1 + s2),
+            "attn": lp(np.tanh(g2), 1 + s1), "out": lp(np.tanh(g2), 1 + out_scale)}
 
 
 def joint_layout(vlm_image_mask, n_target=4096, grid=(64, 64)):
