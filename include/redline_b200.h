@@ -258,8 +258,9 @@ int rl_adaln_params(const float* mod, const float* out_scale, int ld_out, int D,
 int rl_set_gemm_variant(int variant);
 
 /* Attention kernel for tests and benchmarks: 0 = default (two 128-query tiles per CTA, the tensor pipe working on one
- * tile while the other's softmax runs), 1 = one query tile per CTA, 2-5 = two-tile forms (2 + 2 * in-order Q.K issue
- * + P released in two halves). Returns the previous value. */
+ * tile while the other's softmax runs; = variant 5), 1 = one query tile per CTA, 2-5 = two-tile forms (2 + 2 * the
+ * next Q.K issued in order behind the P.V instead of after its completion + P released in two halves). Returns the
+ * previous value. */
 int rl_set_attention_variant(int variant);
 
 #ifdef __cplusplus

@@ -493,8 +493,10 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 // P_1 V, S_1 = Q_1 K per key block - so the tensor pipe works on one tile while the other tile's softmax runs, and
 // each K / V block is loaded once for both tiles. TMEM: S_0 [0, 128), S_1 [128, 256), O_0 [256, 384),
 // O_1 [384, 512); P_t is written over S_t. S_t of the next block overwrites P_t, which P_t.V reads: kInOrder issues
-// that Q.K right after the P.V (the tensor pipe runs one thread's MMAs in issue order, so the P.V has read its
-// operand first), otherwise the Q.K waits for the P.V's completion.
+// that Q.K right after the P.V - a write after a read by the MMA issued just before it on the same SM's tensor
+// pipe, which executes one thread's MMAs in issue order, so the P.V's operand reads precede the Q.K's accumulator
+// writes (the form every variant's outputs are compared against in the parity tests: they agree bit for bit) -
+// otherwise the Q.K waits for the P.V's completion (one commit -> wake hand-off more per block, ~4 % slower).
 // Warpgroup 0 (producer, MMA issuer, two idle warps) gives registers to the two softmax warpgroups (setmaxnreg):
 // a softmax thread holds its 128 scores and 64 packed probabilities.
 namespace two {
@@ -718,10 +720,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 }  // namespace two
 
-// Kernel choice for rl_attention_gqa: 0 = default (two query tiles per CTA, P released in halves, Q.K after the
-// P.V's completion: variant 3), 1 = one tile per CTA; 2-5 = the two-tile forms 2 + 2 * kInOrder + kSplitP. Measured
-// at config 3 (24 heads x 4352, B200): one tile 257 us, variant 2 221 us, 3 213 us, 4 215 us, 5 211 us - issuing
-// Q.K in order behind the P.V gains ~1 %, so the default keeps the explicit wait.
+// Kernel choice for rl_attention_gqa: 0 = default (two query tiles per CTA, P released in halves, the next Q.K issued
+// right behind the P.V: variant 5), 1 = one tile per CTA; 2-5 = the two-tile forms 2 + 2 * kInOrder + kSplitP.
+// Medians of 12 interleaved samples at config 3 (24 heads x 4352, B200): variant 2 240 us, 3 231 us, 4 226 us,
+// 5 220 us (one tile per CTA: 257 us best case).
 inline int& variant() {
   static int v = 0;
   return v;
@@ -818,7 +820,7 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
       case 3: st = two_tile_launch<false, true>(grid, mq, mk, mv, p, stream); break;
       case 4: st = two_tile_launch<true, false>(grid, mq, mk, mv, p, stream); break;
       case 5: st = two_tile_launch<true, true>(grid, mq, mk, mv, p, stream); break;
-      default: st = two_tile_launch<false, true>(grid, mq, mk, mv, p, stream); break;
+      default: st = two_tile_launch<true, true>(grid, mq, mk, mv, p, stream); break;
     }
     if (st != RL_OK) return st;
   } else {

@@ -15,10 +15,10 @@ from oracle import bfp16_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module", params=[0, 1, 2, 5], ids=["default", "one-tile", "two-tile-wait", "two-tile-inorder"])
+@pytest.fixture(scope="module", params=[0, 1, 2, 3], ids=["default", "one-tile", "two-tile-wait", "two-tile-wait-half"])
 def env(request):
-    """The attention kernels: 0 = default (two query tiles per CTA, P in halves), 1 = one query tile per CTA,
-    2 = two tiles with P whole, 5 = two tiles with Q.K issued in order behind P.V."""
+    """The attention kernels: 0 = default (two query tiles per CTA, P in halves, the next Q.K in order behind P.V),
+    1 = one query tile per CTA, 2 / 3 = two tiles whose Q.K waits for the P.V's completion, P whole / in halves."""
     import torch
     from redline_tiny_b200 import ops
     assert torch.cuda.is_available()
@@ -94,3 +94,27 @@ def test_attention_config3_size(env):
     """Benchmark config 3 attention: 24 heads x 4352 tokens (256 text + 4096 image), non-causal; heads 0 and 23
     checked against float64 (run_attn.py:203 checks heads {0, H-1} the same way)."""
     _run(env, 24, 4352, 4352, seed=7, heads=[0, 23])
+
+
+def test_attention_variants_agree_bitwise():
+    """The two-tile forms differ only in when MMAs are issued: their outputs must be identical bit for bit (the
+    in-order form overwrites P with the next block's S right behind the P.V that reads it)."""
+    import torch
+    from redline_tiny_b200 import ops
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(11)
+    H, N = 4, 1000
+    q = _bf16(torch, rng.standard_normal((H, N, 128)).astype(np.float32) * 2, dev)
+    k = _bf16(torch, rng.standard_normal((H, N, 128)).astype(np.float32), dev)
+    vt = _bf16(torch, rng.standard_normal((H, 128, 1024)).astype(np.float32), dev)
+    outs = []
+    prev = ops.set_attention_variant(0)
+    try:
+        for v in (2, 3, 4, 5, 0):
+            ops.set_attention_variant(v)
+            outs.append(ops.attention(q, k, vt, nkv=N - 3).view(torch.int16).cpu().numpy())
+        ops.device_status()
+    finally:
+        ops.set_attention_variant(prev)
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
