@@ -250,6 +250,24 @@ int rl_sinusoidal_embed(float t0, float t1, const float* freqs, int half, float*
 int rl_adaln_params(const float* mod, const float* out_scale, int ld_out, int D, uint16_t* first, uint16_t* mlp,
                     uint16_t* attn, uint16_t* out, rl_stream_t stream);
 
+/* The reference's NPU attention formats, for the QKV-post and attention artifacts of its DiT (forward.py:209-412):
+ * per head h and 64-token tile t, Q[h][t] = to_bfp16(a_layout(Q_h tile, 64, 128)) and KV[h][t] = [K | V] with
+ * K = to_bfp16(b_layout(K_tile^T, 128, 64)), V = to_bfp16(b_layout(V_tile, 64, 128)) (run_attn.py:29-35, 82-92),
+ * 9216 bytes per tile.
+ * rl_npu_qkv_pack: from q, k (H, 64T, 128) and vt (H, 128, ldv) bf16 -> q_out (H, T, 9216 B), kv_out (H, T, 2, 9216 B).
+ * rl_npu_q_unpack: Q tiles [tile0, tile0 + ntiles) of each head (tiles_per_head in the buffer) -> q (H, 64 ntiles, 128).
+ * rl_npu_kv_unpack: K/V tiles [tile0, tile0 + ntiles) of each head -> keys key0 .. key0 + 64 ntiles of k (H, nk, 128)
+ *   and vt (H, 128, ldv) (key0 % 8 == 0, nk <= ldv, ldv % 8 == 0).
+ * rl_npu_qkv_tables: the QKV-post table (T, 8448) bf16 (run_qkv.qkv_tables, run_qkv.py:60-72) -> rope_cs (64T, 64, 2)
+ *   float (cos, sin per row and rotary pair), w_q, w_k (128 floats each). */
+int rl_npu_qkv_pack(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int T,
+                    uint8_t* q_out, uint8_t* kv_out, rl_stream_t stream);
+int rl_npu_q_unpack(const uint8_t* q_in, int H, int tiles_per_head, int tile0, int ntiles, uint16_t* q,
+                    rl_stream_t stream);
+int rl_npu_kv_unpack(const uint8_t* kv_in, int H, int tiles_per_head, int tile0, int ntiles, int64_t key0,
+                     int64_t nk, int64_t ldv, uint16_t* k, uint16_t* vt, rl_stream_t stream);
+int rl_npu_qkv_tables(const uint16_t* tables, int T, float* rope_cs, float* w_q, float* w_k, rl_stream_t stream);
+
 /* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
  * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel

@@ -48,6 +48,10 @@ SIGNATURES = {
     "rl_matvec_f32": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "rl_sinusoidal_embed": (_I, [ctypes.c_float, ctypes.c_float, _P, _I, _P, _P]),
     "rl_adaln_params": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
+    "rl_npu_qkv_pack": (_I, [_P, _P, _P, _I64, _I, _I, _P, _P, _P]),
+    "rl_npu_q_unpack": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "rl_npu_kv_unpack": (_I, [_P, _I, _I, _I, _I, _I64, _I64, _I64, _P, _P, _P]),
+    "rl_npu_qkv_tables": (_I, [_P, _I, _P, _P, _P, _P]),
 }
 
 

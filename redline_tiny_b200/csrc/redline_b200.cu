@@ -7,3 +7,4 @@
 #include "rl_attn.cu"
 #include "rl_conv.cu"
 #include "rl_adaln.cu"
+#include "rl_npu.cu"

@@ -9,12 +9,22 @@ artifact family maps onto the B200 kernels through the C ABI:
   GEMM ("atb3d2-*", "q-atb3k-*", "vlm-gemm-*")  [A, B, C]       forward.py:194-197  (C in ATB order, bfp16)
   up + SwiGLU ("atb3sw2-*", "vlm-upsw*")        [A, B_up, H]    forward.py:250      (H as the down GEMM's A)
   ln_mod ("glue-ln-m{M}-s{S}")                  [x, br, p, x', A]  forward.py:249    (rows < 128 S use row 1)
+  QKV post ("glue-qkv*")                        [C_qkv, tabs, Q, KV]  forward.py:246 (per-head 64-token tiles)
+  attention ("attn32o-*", "attn32q-*")          [Q, KV, (KV_prefix | LIM), O]  forward.py:251, 365-376, 613
 
+Q and KV hold the reference's attention formats (run_attn.py:29-35, 82-92: Q tiles a_layout(., 64, 128), K tiles
+b_layout(K^T, 128, 64), V tiles b_layout(V, 64, 128), bfp16); O is the out-projection's A operand. The attention
+forms, as forward.py uses them (the artifacts' tile ranges are fixed by their builds; here they follow from the
+name and the buffer sizes):
+  attn32o-*-s-*-pf-nk{NK}-nkv{NKV}  [Q, KV_t, KV_p, O]  cached steps: every Q tile over [all of KV_t | KV_p tiles
+                                                        0 ..], NK keys, the first NKV valid
+  attn32o-*-s-*-tr-nk{NK}-nkv{NKV}  [Q, KV, KV_p, O]    step 1 target: Q / KV tiles of the 4096 target rows (from
+                                                        row 4224 at M = 8704, 512 at M = 4608) over [those | KV_p 0 ..]
+  attn32o-*-a-*-tr-nk{NK}-nkv{NKV}  [Q, KV, O]          reference-image rows: Q tiles 0..63 over KV tiles 0 ..
+  attn32q-*-nk{NK}-pt{PT}           [Q, LIM, KV, O]     up to 64 rows per head over KV tiles 0 .. with per-row key
+                                                        limits (LIM: int32 at the start of the buffer, run_attn.pack_lim)
 Shapes come from the buffer sizes (the reference fixes them per artifact). Packed weights are repacked once into the
-native tile format and cached per weight buffer, like the reference's resident `Weights` (forward.py:175-191). The
-QKV-post and attention artifacts use NPU-specific tile orders (per-64-token Q / K / V tiles, kernels/glue/qkv_post.cc,
-kernels/attn/attn_bfp.cc) and are not mapped: on B200 the DiT runs through redline_tiny_b200.dit, which keeps Q, K, V
-in row-major head-major buffers.
+native tile format and cached per weight buffer, like the reference's resident `Weights` (forward.py:175-191).
 """
 
 import math
@@ -45,10 +55,12 @@ class Device:
         elif art.startswith("glue-ln"):
             m = re.search(r"-s(\d+)", art)
             self._ln_mod(*args, row_split=128 * int(m.group(1)) if m else 0)
+        elif art.startswith("glue-qkv"):
+            self._qkv_post(*args)
+        elif art.startswith(("attn32o", "attn32q")):
+            self._attention(art, args)
         else:
-            raise NotImplementedError(
-                f"artifact {art!r}: the NPU's QKV-post / attention tile formats are not mapped; run the DiT with "
-                "redline_tiny_b200.dit on B200")
+            raise NotImplementedError(f"artifact {art!r} is not mapped onto the B200 kernels")
         self.t_wall[op] += time.perf_counter() - t
         self.calls[op] += 1
 
@@ -104,6 +116,110 @@ class Device:
                x1.data_ptr(), y.data_ptr(), None, s)
         L.call("rl_permute_bf16", x1.data_ptr(), L.RL_ROWMAJOR, xo.data_ptr(), L.RL_C_ATB, M, D, s)
         L.call("rl_quantize_bfp16", y.data_ptr(), L.RL_BF16, M, D, L.RL_A_LAYOUT, a.data_ptr(), None, s)
+
+    # -- QKV post and attention in the NPU tile formats ------------------------------------------------------------
+    def _qkv_post(self, c_qkv, tabs, q, kv):
+        """C_qkv (bfp16, ATB order, M x 3 HID) -> per-head RMSNorm * w, RoPE on adjacent pairs (tables decoded from
+        the reference's qkv_tables rows) -> Q / KV in the attention formats (run_qkv.py:41-79)."""
+        c, qb, kvb = (t.view(torch.uint8).reshape(-1) for t in (c_qkv, q, kv))
+        tb = tabs.view(torch.bfloat16).reshape(-1)
+        T = tb.numel() // TAB_ROW
+        M = 64 * T
+        n3 = c.numel() * 8 // 9 // M
+        H = n3 // 3 // 128
+        if tb.numel() != T * TAB_ROW or n3 * M * 9 // 8 != c.numel() or n3 != 3 * 128 * H:
+            raise ValueError("qkv_post: C_qkv / table sizes do not match")
+        if qb.numel() != H * T * TILE_BYTES or kvb.numel() != 2 * H * T * TILE_BYTES:
+            raise ValueError(f"qkv_post: Q / KV buffers must hold {H} heads x {T} tiles")
+        s = torch.cuda.current_stream().cuda_stream
+        dev = c.device
+        cdq = ops.dequantize_bfp16(c, M, n3, layout="c_atb", dtype=torch.bfloat16)
+        cs = torch.empty(M, 64, 2, dtype=torch.float32, device=dev)
+        wq = torch.empty(128, dtype=torch.float32, device=dev)
+        wk = torch.empty(128, dtype=torch.float32, device=dev)
+        L.call("rl_npu_qkv_tables", tb.data_ptr(), T, cs.data_ptr(), wq.data_ptr(), wk.data_ptr(), s)
+        ldv = (M + 127) // 128 * 128
+        qq = torch.empty(H, M, 128, dtype=torch.bfloat16, device=dev)
+        kk = torch.empty(H, M, 128, dtype=torch.bfloat16, device=dev)
+        vt = torch.zeros(H, 128, ldv, dtype=torch.bfloat16, device=dev)
+        L.call("rl_qkv_post", cdq.data_ptr(), cs.data_ptr(), wq.data_ptr(), wk.data_ptr(), M, H, qq.data_ptr(),
+               kk.data_ptr(), vt.data_ptr(), ldv, s)
+        L.call("rl_npu_qkv_pack", qq.data_ptr(), kk.data_ptr(), vt.data_ptr(), ldv, H, T, qb.data_ptr(),
+               kvb.data_ptr(), s)
+
+    @staticmethod
+    def _tiles(buf, H, per_tile):
+        n = buf.numel()
+        if n % (H * per_tile):
+            raise ValueError(f"buffer of {n} bytes is not {H} heads of whole tiles")
+        return n // (H * per_tile)
+
+    def _attention(self, art, args):
+        """The attention artifacts (forms in the module docstring): unpack the Q / K / V tiles each form reads, run
+        rl_attention_gqa (Q already carries log2(e) / sqrt(128)), write O as the out-projection's bfp16 A operand."""
+        s = torch.cuda.current_stream().cuda_stream
+        mo = re.match(r"attn32o-v\d+-([sa])-h(\d+)-t\d+-(pf|tr)-nk(\d+)-nkv(\d+)", art)
+        mq = re.match(r"attn32q-v\d+-t\d+-nk(\d+)-pt(\d+)", art)
+        if mo:
+            split, H, mode, NK, NKV = mo.group(1), int(mo.group(2)), mo.group(3), int(mo.group(4)), int(mo.group(5))
+        elif mq:
+            H, NK, NKV, split, mode = 32, int(mq.group(1)), int(mq.group(1)), "q", "small"
+        else:
+            raise NotImplementedError(f"attention artifact {art!r}: unknown form")
+        bufs = [t.view(torch.uint8).reshape(-1) for t in args]
+        if NK % 64 or not 0 < NKV <= NK:
+            raise ValueError(f"{art}: NK must be a multiple of 64 and 0 < NKV <= NK")
+        row_limit = None
+        if split == "s":
+            qb, kvt, kvp, ob = bufs
+            Tq, Tt, Tp = (self._tiles(b, H, u) for b, u in ((qb, TILE_BYTES), (kvt, 2 * TILE_BYTES),
+                                                            (kvp, 2 * TILE_BYTES)))
+            if mode == "pf":
+                q_rng, kv_rngs = (0, Tq), [(kvt, Tt, 0, Tt)]
+                npre = NK // 64 - Tt
+            else:
+                t0 = {8704: 4224, 4608: 512}.get(64 * Tq)
+                if t0 is None:
+                    raise ValueError(f"{art}: target rows of a {64 * Tq}-row step-1 layout are not known")
+                q_rng, kv_rngs = (t0 // 64, 64), [(kvt, Tt, t0 // 64, 64)]
+                npre = NK // 64 - 64
+            if npre < 0 or npre > Tp:
+                raise ValueError(f"{art}: {npre} prefix tiles outside the {Tp}-tile prefix buffer")
+            if npre:
+                kv_rngs.append((kvp, Tp, 0, npre))
+        elif split == "a":
+            qb, kv, ob = bufs
+            Tq, Tk = self._tiles(qb, H, TILE_BYTES), self._tiles(kv, H, 2 * TILE_BYTES)
+            q_rng, kv_rngs = (0, min(64, Tq)), [(kv, Tk, 0, NK // 64)]
+        else:
+            qb, lim, kv, ob = bufs
+            Tq, Tk = self._tiles(qb, H, TILE_BYTES), self._tiles(kv, H, 2 * TILE_BYTES)
+            if Tk != int(mq.group(2)):
+                raise ValueError(f"{art}: the K/V buffer holds {Tk} tiles per head, the artifact reads {mq.group(2)}")
+            q_rng, kv_rngs = (0, Tq), [(kv, Tk, 0, NK // 64)]
+            row_limit = lim[:4 * 64 * Tq].view(torch.int32)
+        dev = bufs[0].device
+        nq = 64 * q_rng[1]
+        q = torch.empty(H, nq, 128, dtype=torch.bfloat16, device=dev)
+        L.call("rl_npu_q_unpack", qb.data_ptr(), H, Tq, q_rng[0], q_rng[1], q.data_ptr(), s)
+        k = torch.empty(H, NK, 128, dtype=torch.bfloat16, device=dev)
+        vt = torch.empty(H, 128, NK, dtype=torch.bfloat16, device=dev)
+        key0 = 0
+        for buf, tpl, t0, n in kv_rngs:
+            L.call("rl_npu_kv_unpack", buf.data_ptr(), H, tpl, t0, n, key0, NK, NK, k.data_ptr(), vt.data_ptr(), s)
+            key0 += 64 * n
+        if key0 != NK:
+            raise ValueError(f"{art}: the tile ranges give {key0} keys, the artifact reads {NK}")
+        rows_out = ob.numel() * 8 // 9 // (H * 128)
+        if rows_out * H * 128 * 9 // 8 != ob.numel() or rows_out < nq or rows_out % 128:
+            raise ValueError(f"{art}: O must hold a multiple of 128 rows >= {nq} of {H} heads")
+        o = torch.zeros(rows_out, H * 128, dtype=torch.bfloat16, device=dev)
+        ops.attention(q, k, vt, nkv=NKV, row_limit=row_limit, scale_log2=1.0, out=o[:nq], ldo=H * 128)
+        L.call("rl_quantize_bfp16", o.data_ptr(), L.RL_BF16, rows_out, H * 128, L.RL_A_LAYOUT, ob.data_ptr(), None, s)
+
+
+TILE_BYTES = 64 * 128 // 8 * 9    # one 64-token Q / K / V tile
+TAB_ROW = 128 * 64 + 2 * 128      # QKV-post table entries per 64-row tile (run_qkv.TAB)
 
 
 def gemm(npu, w, op, M, a, c, block=None):

@@ -212,6 +212,24 @@ def main(ref_root):
     out["vconv_ref"] = vo.conv_ref(xv, wv, bv)
     out["vconv1_ref"] = vo.conv_ref(xv, wv[:, :, 1:2, 1:2], bv)
 
+    # --- the NPU attention formats (run_attn.py:29-35, 82-92) and the QKV-post table (run_qkv.py:60-72), own generator
+    import run_attn as ra
+    rn = np.random.default_rng(21)
+    Hn, Tn = 2, 2
+    qn, kn, vn = (rn.standard_normal((Hn, 64 * Tn, 128)).astype(bfloat16).astype(np.float32) for _ in range(3))
+    out["npu_q"], out["npu_k"], out["npu_v"] = qn, kn, vn
+    out["npu_qpack"] = np.concatenate([nl.to_bfp16(nl.a_layout(qn[h], 64, 128)) for h in range(Hn)])
+    out["npu_kvpack"] = np.concatenate([ra.pack_kv(kn[h], vn[h], 64) for h in range(Hn)])
+    ang = rn.uniform(-np.pi, np.pi, (64 * Tn, 64))
+    cosn = np.cos(ang).astype(bfloat16).astype(np.float32)
+    sinn = np.sin(ang).astype(bfloat16).astype(np.float32)
+    wqn = (rn.standard_normal(128) * rq.C_LOG2).astype(bfloat16).astype(np.float32)
+    wkn = (1 + 0.1 * rn.standard_normal(128)).astype(bfloat16).astype(np.float32)
+    out["npu_cos"], out["npu_sin"], out["npu_wq"], out["npu_wk"] = cosn, sinn, wqn, wkn
+    out["npu_tab"] = rq.qkv_tables(cosn, sinn, wqn, wkn).view(np.uint16)
+    limn = rn.integers(0, 250, 64).astype(np.int32)
+    out["npu_lim"], out["npu_limpack"] = limn, ra.pack_lim(limn, 64, 64)
+
     dst = Path(__file__).with_name("golden.npz")
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size / 1e3:.0f} KB, {len(out)} arrays)")

@@ -141,3 +141,24 @@ def test_vae_conv_oracle_and_weight_blocks(golden):
     assert np.allclose(VO.conv_ref(x, w[:, :, 1:2, 1:2], b), golden["vconv1_ref"], rtol=0, atol=1e-12)
     ref_w = VO.unpack_vconv_weights(golden["vconv_packed"], 32, 16, 3, 16, 16)
     assert np.array_equal(VO.decode_conv_b(w), ref_w)
+
+
+def test_npu_attention_formats(golden):
+    """The oracle's Q / [K|V] tile packing, QKV-post table and key-limit buffer reproduce the reference's bytes
+    (run_attn.pack_kv / a_layout Q tiles, run_qkv.qkv_tables, run_attn.pack_lim)."""
+    from oracle import npu_oracle as N
+    q, k, v = golden["npu_q"], golden["npu_k"], golden["npu_v"]
+    assert np.array_equal(N.q_pack(q), golden["npu_qpack"])
+    assert np.array_equal(N.kv_pack(k, v), golden["npu_kvpack"])
+    # decoding gives each value's bfp16 rounding (re-encoding is not byte-identical: a block whose negative maximum
+    # rounds to -128 decodes to -2^(E - 126), which encodes with exponent E + 1)
+    qd = N.q_unpack(golden["npu_qpack"], 2)
+    kd, vd = N.kv_unpack(golden["npu_kvpack"], 2)
+    for got, ref in ((qd, q), (kd, k), (vd, v)):
+        assert np.abs(got - ref).max() <= 2.0 ** -6 * np.abs(ref).max()
+    tab = N.tables(golden["npu_cos"], golden["npu_sin"], golden["npu_wq"], golden["npu_wk"])
+    assert np.array_equal(tab, golden["npu_tab"])
+    cos, sin, wq, wk = N.tables_decode(golden["npu_tab"])
+    for got, name in ((cos, "npu_cos"), (sin, "npu_sin"), (wq, "npu_wq"), (wk, "npu_wk")):
+        assert np.array_equal(got, golden[name]), name
+    assert np.array_equal(N.lim_pack(golden["npu_lim"]), golden["npu_limpack"])
