@@ -208,6 +208,41 @@ def _event_ms(fn, n, w, stream):
     return e0.elapsed_time(e1) / n
 
 
+def measure_next_rows(dev, stream, seed):
+    """The paths beyond configs 1-5 (CUDA events, seeded synthetic inputs, random N(0, 0.02) weights): the VAE
+    decoder's 3x3 convolutions at two of its stages (vae_decode.py:311-348: 1152 channels at 128^2, 288 at 512^2 -
+    K = 9 * 288 padded to 2624) and one Qwen3-VL-8B decoder layer at the reference's M = 1536 rows (vlm_run.py:396-431,
+    causal GQA over 1500 valid rows)."""
+    import math
+    import torch
+    from redline_tiny_b200 import ops, vlm
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 5)
+    res = {}
+    for H, C in ((128, 1152), (512, 288)):
+        x = ops.quantize_bfp16(torch.randn((H * H, C), generator=g, device=dev), want_bytes=False)[1].view(H, H, C)
+        w = torch.randn((C, C, 3, 3), generator=g, device=dev) * 0.02
+        pw, bias, taps = ops.conv_weight(w, torch.randn(C, generator=g, device=dev) * 0.01)
+        y = torch.empty((H, H, pw.N), dtype=torch.bfloat16, device=dev)
+        ms = _event_ms(lambda: ops.conv2d(x, pw, bias, taps, out=y), 10, 3, stream)
+        fl = 2.0 * H * H * 9 * C * C
+        res[f"vae_conv3_{H}x{H}x{C}"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "GFLOP": fl / 1e9,
+                                         "gather_bytes": H * H * ops.conv_k(C, 3) * 2}
+        del x, w, pw, y
+    cfg = vlm.LMConfig()
+    M, valid = 1536, 1500
+    lm = vlm.LM(cfg, vlm.random_lm_weights(cfg, seed=seed), M, device=dev)
+    ang = torch.rand((M, 64), generator=g, device=dev) * 2 * math.pi
+    lm.set_positions(torch.cos(ang).cpu(), torch.sin(ang).cpu(), valid)
+    lm.load_x(torch.randn((M, cfg.hidden), generator=g, device=dev))
+    ms = _event_ms(lambda: lm.layer(0), 10, 3, stream)
+    fl = cfg.flop_per_layer(M, valid)
+    res["vlm_layer_m1536"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "GFLOP": fl / 1e9}
+    del lm
+    torch.cuda.empty_cache()
+    return res
+
+
 def measure_configs(dev, stream, ws, seed):
     """The other benchmark configs (2-5) on this GPU (every rank runs its own copy: data-parallel), CUDA-event timed.
     Inputs are seeded synthetic tensors of the configs' shapes; weights N(0, 0.02)."""
@@ -278,6 +313,7 @@ def measure_configs(dev, stream, ws, seed):
                           "TFLOP_per_step": cfg.flop_per_step() / 1e12, "weights_GB": 5.44}
     del model
     torch.cuda.empty_cache()
+    out["next_rows"] = measure_next_rows(dev, stream, seed)
     if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1 (NCCL all-reduce of bf16 partials)
         import torch.distributed as dist
         rank = dist.get_rank()

@@ -225,9 +225,10 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
  * artifacts (kernels/vae/vconv.cc:1-17, redline/vae_decode.py:168-194; weights packed by vae_ops.pack_vconv,
  * vae_ops.py:44-61) and is checked against vae_ops.conv_ref (vae_ops.py:64-75).
  * x: (H, W, Cin) bf16 holding bfp16-exact values (rl_quantize_bfp16's decoded output of the (H * W, Cin) matrix);
- * w_native: the native tiles of B = [(dy * taps + dx) * Cin + ci][co] = w[co][ci][dy][dx] (K = taps^2 * Cin, a
- * multiple of 64; N = Cout, a multiple of 128 - pad smaller outputs); bias: bf16 [Cout] or NULL; out: (H, W, Cout)
- * bf16. workspace: rl_conv2d_workspace(H, W, Cin, taps) bytes (the im2col rows of the 3x3 conv; 0 for 1x1).
+ * Cin % 8 == 0. w_native: the native tiles of B = [(dy * taps + dx) * Cin + ci][co] = w[co][ci][dy][dx] with zero rows
+ * after the last tap up to K = taps^2 * Cin rounded up to a multiple of 64; N = Cout, a multiple of 128 (pad smaller
+ * outputs with zero columns); bias: bf16 [Cout] or NULL; out: (H, W, Cout) bf16. workspace:
+ * rl_conv2d_workspace(H, W, Cin, taps) bytes (the gathered rows of K columns; 0 for a 1x1 conv with Cin % 64 == 0).
  */
 size_t rl_conv2d_workspace(int H, int W, int Cin, int taps);
 int rl_conv2d_bfp16(const uint16_t* x, int H, int W, int Cin, const uint8_t* w_native, int Cout, int taps,
@@ -272,7 +273,8 @@ int rl_npu_qkv_tables(const uint16_t* tables, int T, float* rope_cs, float* w_q,
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
  * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel
  * (tcgen05.mma cta_group::2 over a cluster of two CTAs) with A in shared memory / TMEM; tuning codes
- * 1000*P + 100*G + 10*V + S also select the decode split and the pipeline depth. Returns the previous value. */
+ * 1000*P + 100*G + 10*V + S (1313, 1125, 2125, 1224, 2224, 1333, 1234, 1346, 1448, 2248) also select the decode split
+ * and the pipeline depth. Returns the previous value. */
 int rl_set_gemm_variant(int variant);
 
 /* Attention kernel for tests and benchmarks: 0 = default (two 128-query tiles per CTA, the tensor pipe working on one

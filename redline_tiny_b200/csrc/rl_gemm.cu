@@ -62,6 +62,10 @@ struct Cfg {
   static_assert(V == kSmemA || 256 + S * (BK / 2) <= 512, "TMEM: one D buffer + S A stages");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(S <= 8 && G >= 1 && G <= 4 && (P == 1 || P == 2), "config");
+  // A decoder group takes the stages s with s % G == its group, so that it waits on every phase of those stages'
+  // load barriers in turn. With S % G != 0 a group would return to a stage only every lcm(S, G) K steps, and its
+  // parity wait could be satisfied by a phase two behind the one it needs when a later load lands first.
+  static_assert(S % G == 0, "the decoder groups must own whole stages");
 };
 
 struct Params {
@@ -433,6 +437,10 @@ struct Cfg {
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(V == kSmemA || 256 + S * (BK / 2) <= 512, "TMEM: accumulator + A stages");
   static_assert(S <= 8 && G >= 1 && G <= 4 && (P == 1 || P == 2), "config");
+  // A decoder group takes the stages s with s % G == its group, so that it waits on every phase of those stages'
+  // load barriers in turn. With S % G != 0 a group would return to a stage only every lcm(S, G) K steps, and its
+  // parity wait could be satisfied by a phase two behind the one it needs when a later load lands first.
+  static_assert(S % G == 0, "the decoder groups must own whole stages");
 };
 
 template <int V, int S, int G, int P>
@@ -724,35 +732,35 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   return RL_OK;
 }
 
-// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S; V = 3 / 4 are the
-// 2-SM pair kernel with A in shared memory / TMEM); 0 = default: the pair kernel with A in TMEM (8 stages, decode
-// split in two parts x two groups) when N is a multiple of 256, else the 1-SM kernel with A in TMEM.
+// Kernel variants selectable with rl_set_gemm_variant (code = 1000 * P + 100 * G + 10 * V + S; V = 1 / 2: the 1-SM
+// kernel with A in shared memory / TMEM, V = 3 / 4: the 2-SM pair kernel with A in shared memory / TMEM; every code
+// has S % G == 0). 0 = default: the pair kernel with A in TMEM (8 stages, decode split in two parts x two groups)
+// when N is a multiple of 256, else the 1-SM kernel with A in TMEM (code kDefault1Sm). 1 - 4: one code per kernel
+// form for the tests.
+constexpr int kDefault1Sm = 2224;
 int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) {
   const bool pairable = p.num_w_tiles % 2 == 0;
-  if (code == 0) code = pairable ? 2248 : 1325;
+  if (code == 0) code = pairable ? 2248 : kDefault1Sm;
   switch (code) {
     case 1:
-    case 1213: return launch<kSmemA, 3, 2, 1>(x, p, stream);
+    case 1313: return launch<kSmemA, 3, 3, 1>(x, p, stream);
     case 1125: return launch<kTmemA, 5, 1, 1>(x, p, stream);
-    case 1225: return launch<kTmemA, 5, 2, 1>(x, p, stream);
-    case 2:
-    case 1325: return launch<kTmemA, 5, 3, 1>(x, p, stream);
     case 2125: return launch<kTmemA, 5, 1, 2>(x, p, stream);
-    case 2225: return launch<kTmemA, 5, 2, 2>(x, p, stream);
+    case 1224: return launch<kTmemA, 4, 2, 1>(x, p, stream);
+    case 2:
     case 2224: return launch<kTmemA, 4, 2, 2>(x, p, stream);
     default: break;
   }
-  if (code == 3 || code == 4 || code == 1335 || code == 1235 || code == 2235 || code == 1348 || code == 1448 ||
-      code == 2248) {
+  if (code == 3 || code == 4 || code == 1333 || code == 1234 || code == 1346 || code == 1448 || code == 2248) {
     if (!pairable) return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: the pair kernel needs N %% 256 == 0");
     switch (code) {
-      case 1235: return launch_pair<kSmemA, 5, 2, 1>(x, p, stream);
-      case 2235: return launch_pair<kSmemA, 5, 2, 2>(x, p, stream);
+      case 3:
+      case 1333: return launch_pair<kSmemA, 3, 3, 1>(x, p, stream);
+      case 1234: return launch_pair<kSmemA, 4, 2, 1>(x, p, stream);
+      case 1346: return launch_pair<kTmemA, 6, 3, 1>(x, p, stream);
       case 4:
-      case 1348: return launch_pair<kTmemA, 8, 3, 1>(x, p, stream);
       case 1448: return launch_pair<kTmemA, 8, 4, 1>(x, p, stream);
-      case 2248: return launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
-      default: return launch_pair<kSmemA, 5, 3, 1>(x, p, stream);
+      default: return launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
     }
   }
   return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);

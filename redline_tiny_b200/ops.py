@@ -214,14 +214,19 @@ def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo
     return out
 
 
+def conv_k(cin, taps):
+    """The conv GEMM's K: taps^2 * Cin rounded up to a multiple of 64 (zero rows after the last tap)."""
+    return (taps * taps * cin + 63) // 64 * 64
+
+
 def conv_weight(w, bias=None, cout_pad=128):
     """Conv weight (Cout, Cin, k, k), k = 3 or 1, on the GPU -> (PackedWeight of B = [(dy, dx, ci)][co], bf16 bias or
-    None, taps). Cout is zero-padded to a multiple of `cout_pad` (the GEMM's N tile)."""
+    None, taps). K is zero-padded to conv_k(Cin, k), Cout to a multiple of `cout_pad` (the GEMM's N tile)."""
     _check_cuda(w, bias)
     cout, cin, k, _ = w.shape
     n = (cout + cout_pad - 1) // cout_pad * cout_pad
-    B = torch.zeros((k * k * cin, n), dtype=torch.float32, device=w.device)
-    B[:, :cout] = w.float().permute(2, 3, 1, 0).reshape(k * k * cin, cout)
+    B = torch.zeros((conv_k(cin, k), n), dtype=torch.float32, device=w.device)
+    B[:k * k * cin, :cout] = w.float().permute(2, 3, 1, 0).reshape(k * k * cin, cout)
     b = None
     if bias is not None:
         b = torch.zeros(n, dtype=torch.bfloat16, device=w.device)
@@ -233,8 +238,8 @@ def conv2d(x_dq, w, bias, taps, out=None):
     """VAE conv: x_dq (H, W, Cin) bf16 holding bfp16 values -> (H, W, N) bf16 (N = the padded Cout)."""
     _check_cuda(x_dq, w.native, bias, out)
     H, Wd, C = x_dq.shape
-    if w.K != taps * taps * C:
-        raise ValueError(f"conv weight has K = {w.K}, a {taps}x{taps} conv over {C} channels needs {taps * taps * C}")
+    if w.K != conv_k(C, taps):
+        raise ValueError(f"conv weight has K = {w.K}, a {taps}x{taps} conv over {C} channels needs {conv_k(C, taps)}")
     if out is None:
         out = torch.empty((H, Wd, w.N), dtype=torch.bfloat16, device=x_dq.device)
     nbytes = L.lib().rl_conv2d_workspace(H, Wd, C, taps)

@@ -22,7 +22,11 @@ def env():
 
 
 @pytest.mark.parametrize("H,W,Cin,Cout,k", [(24, 20, 64, 128, 3), (24, 20, 64, 128, 1), (17, 9, 128, 3, 3),
-                                            (64, 64, 128, 256, 3), (32, 32, 512, 512, 1)])
+                                            (64, 64, 128, 256, 3), (32, 32, 512, 512, 1),
+                                            # the VAE decoder's 288- and 144-channel stages and conv_out (144 -> 4):
+                                            # 9 * Cin not a multiple of 64, and a 1x1 conv that needs the gather
+                                            (20, 18, 288, 288, 3), (16, 12, 144, 144, 3), (16, 12, 144, 4, 3),
+                                            (10, 11, 40, 128, 1)])
 def test_conv2d(env, H, W, Cin, Cout, k):
     torch, ops, dev = env
     rng = np.random.default_rng(H * W + Cin + k)
@@ -47,6 +51,6 @@ def test_conv2d_rejects_bad_shapes(env):
         ops.conv2d(torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev), pw, None, 3)
     x = torch.zeros((4, 4, 12), dtype=torch.bfloat16, device=dev)
     ws = torch.empty(4 * 4 * 9 * 12 * 2, dtype=torch.uint8, device=dev)
-    with pytest.raises(L.RedlineError):     # the C ABI: 9 * 12 is not a multiple of 64
+    with pytest.raises(L.RedlineError):     # the C ABI: 12 channels are not whole bfp16 blocks of 8
         L.call("rl_conv2d_bfp16", x.data_ptr(), 4, 4, 12, pw.native.data_ptr(), 128, 3, None, x.data_ptr(),
                ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
