@@ -216,6 +216,7 @@ def measure_next_rows(dev, stream, seed):
     import math
     import torch
     from redline_tiny_b200 import ops, vlm
+    from redline_tiny_b200 import _lib as L
     g = torch.Generator(device=dev)
     g.manual_seed(seed + 5)
     res = {}
@@ -240,6 +241,7 @@ def measure_next_rows(dev, stream, seed):
     res["vlm_layer_m1536"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "GFLOP": fl / 1e9}
     del lm
     torch.cuda.empty_cache()
+    L.device_status()      # raises if any kernel recorded a device-side error (e.g. a bounded wait that ran out)
     return res
 
 
@@ -331,6 +333,7 @@ def measure_configs(dev, stream, ws, seed):
                                       "all_reduce_dtype": "bf16"}
         del tp_model
         torch.cuda.empty_cache()
+    L.device_status()      # raises if any kernel recorded a device-side error
     return out
 
 
