@@ -721,7 +721,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace two
 
 // Kernel choice for rl_attention_gqa: 0 = default (two query tiles per CTA, P released in halves, the next Q.K issued
-// right behind the P.V: variant 5), 1 = one tile per CTA; 2-5 = the two-tile forms 2 + 2 * kInOrder + kSplitP.
+// right behind the P.V: variant 5 - or the one-tile kernel when its grid needs fewer wave-cycles, as with the few
+// heads per GPU of tensor parallelism), 1 = one tile per CTA; 2-5 = the two-tile forms 2 + 2 * kInOrder + kSplitP.
 // Medians of 12 interleaved samples at config 3 (24 heads x 4352, B200): variant 2 240 us, 3 231 us, 4 226 us,
 // 5 220 us (one tile per CTA: 257 us best case).
 inline int& variant() {
@@ -812,7 +813,15 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
     RL_TRY_CUDA(cudaMemset2DAsync(o, ldo * 2, 0, static_cast<size_t>(H) * HD * 2, Nq, stream));
     return RL_OK;
   }
-  const int v = variant();
+  int v = variant();
+  if (v == 0) {
+    // The two-tile kernel runs a key block of both tiles in ~3300 cycles, the one-tile kernel a key block of its tile
+    // in ~2150 (clock64 traces at config 3); with few heads the two-tile grid fills a fraction of a wave, so take the
+    // form with the fewer estimated wave-cycles.
+    const int64_t sms = sm_count();
+    const int64_t n2 = (Nq + 2 * BQ - 1) / (2 * BQ) * H, n1 = (Nq + BQ - 1) / BQ * H;
+    if ((n1 + sms - 1) / sms * 2150 < (n2 + sms - 1) / sms * 3300) v = 1;
+  }
   if (v != 1) {
     const dim3 grid(static_cast<unsigned>((Nq + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(H));
     switch (v) {
