@@ -275,6 +275,24 @@ def measure_configs(dev, stream, ws, seed):
         del xs, c
     out["C5_gemm_sweep_K3072_N12288"] = sweep
     del ws5
+    # the quantiser alone at config 1's X (HBM-bound): bf16 in, bfp16 bytes (row-major blocks) and the decoded bf16
+    # copy the GEMM reads out; inputs rotate over 3 sets of 26.7 MB, outputs over 2 (together above the 126 MB L2)
+    Mq, Kq = 4352, 3072
+    xs = [torch.randn((Mq, Kq), generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+    qs = [torch.empty(Mq * Kq // 8 * 9, dtype=torch.uint8, device=dev) for _ in range(2)]
+    ds = [torch.empty((Mq, Kq), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    iq = [0]
+
+    def fq():
+        i = iq[0] = iq[0] + 1
+        L.call("rl_quantize_bfp16", xs[i % 3].data_ptr(), L.RL_BF16, Mq, Kq, L.RL_ROWMAJOR, qs[i % 2].data_ptr(),
+               ds[i % 2].data_ptr(), stream.cuda_stream)
+    ms = _event_ms(fq, 50, 5, stream)
+    nbytes = Mq * Kq * (2 + 9 / 8 + 2)
+    pk, kind = peaks()
+    out["quantize_c1"] = {"ms": ms, "GB/s": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes,
+                          "frac_of_hbm": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], "peak_kind": kind}
+    del xs, qs, ds
     # config 2: Qwen3-VL SwiGLU MLP, X[512, 4096] -> gate/up [4096, 12288] -> down [12288, 4096]
     M2, K2, F2, N2 = 512, 4096, 12288, 4096
     wu = ops.PackedWeight.from_float(torch.randn((K2, 2 * F2), generator=g, device=dev) * 0.02, swiglu=True)
