@@ -123,6 +123,17 @@ int rl_pack_weights(const void* B, int dtype, int64_t K, int64_t N, int swiglu_i
 int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                     const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream);
 
+/* rl_linear_bfp16 with a caller workspace for split-K: when the pair kernel's grid would fill less than the GPU
+ * (N % 256 == 0, few tiles, long K), K is split into S ranges whose fp32 partials go to the workspace and one
+ * HBM-bound kernel adds them (+ bias) into out. rl_linear_bfp16_workspace(M, K, N, epilogue) gives the bytes
+ * (S * M * N * 4; 0 when no split helps, or for the SwiGLU epilogue); with a smaller workspace, a NULL one or a
+ * non-default kernel variant the call is rl_linear_bfp16. The result differs from the unsplit one only by fp32
+ * summation order. */
+size_t rl_linear_bfp16_workspace(int64_t M, int64_t K, int64_t N, int epilogue);
+int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                       const uint16_t* bias, int epilogue, void* out, int out_dtype, void* workspace,
+                       size_t workspace_bytes, rl_stream_t stream);
+
 /*
  * a9/a13 - the SwiGLU MLP: quantise x (unless x_quantized), H = silu(x @ Bgate) * (x @ Bproj) rounded to bfp16
  * (the up GEMM with the SwiGLU epilogue), out = H @ Bdown. Replaces the up+SwiGLU / down pair of LM._layer
@@ -130,7 +141,8 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
  * (kernels/atb3/mm_bfp_swiglu.cc:88-168) followed by matmul_vectorized_bfp16.
  * x: (M, K) RL_BF16 / RL_F32 (x_quantized=1: bf16 already holding bfp16 values); w_up: native (K, F2) packed with
  * swiglu_interleaved=1, F2 = 2F; w_down: native (F, N); out: (M, N) RL_BF16 or RL_F32.
- * workspace: caller-owned device scratch of rl_swiglu_mlp_workspace(M, K, F, x_quantized) bytes, 256-byte aligned.
+ * workspace: caller-owned device scratch of rl_swiglu_mlp_workspace(M, K, F, x_quantized) bytes, 256-byte aligned
+ * (it includes room for the down GEMM's split-K partials when N = K; a workspace without it runs the down GEMM unsplit).
  */
 size_t rl_swiglu_mlp_workspace(int64_t M, int64_t K, int64_t F, int x_quantized);
 int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up, int64_t F2,

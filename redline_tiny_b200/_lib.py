@@ -31,6 +31,8 @@ SIGNATURES = {
     "rl_weights_from_pack_b": (_I, [_P, _I64, _I64, _I, _P, _P]),
     "rl_pack_weights": (_I, [_P, _I, _I64, _I64, _I, _P, _P]),
     "rl_linear_bfp16": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P]),
+    "rl_linear_bfp16_workspace": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),
+    "rl_linear_bfp16_ws": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P, ctypes.c_size_t, _P]),
     "rl_set_gemm_variant": (_I, [_I]),
     "rl_set_attention_variant": (_I, [_I]),
     "rl_conv2d_workspace": (ctypes.c_size_t, [_I, _I, _I, _I]),

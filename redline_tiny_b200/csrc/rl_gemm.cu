@@ -76,6 +76,8 @@ struct Params {
   int out_f32;           // 1: fp32 output, 0: bf16
   int epilogue;          // RL_EPI_*
   int num_x_tiles, num_w_tiles, num_tiles, KT;
+  int splits;            // pair kernel: K split into this many ranges, fp32 partials split_stride elements apart
+  int64_t split_stride;
 };
 
 struct Barriers {
@@ -95,7 +97,7 @@ __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + _
 // Epilogue of one 16-column chunk of D (16 activation rows x this warp's 32 weight columns): bias, SwiGLU or plain
 // conversion, transposed through the warp's staging buffer into row-major global memory.
 __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&r)[kChunk], uint8_t* st, int lane,
-                                               int q, int wt, int64_t x0, float bias_v) {
+                                               int q, int wt, int64_t x0, float bias_v, int64_t out_off = 0) {
   if (p.epilogue == RL_EPI_SWIGLU) {
     // lanes 0-15 hold the gate of units 16q + lane, lanes 16-31 the proj of the same units. Stage the chunk
     // (16 rows x 32 values, row stride 36 floats: conflict-free both ways), then lane (row = lane & 15,
@@ -143,7 +145,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
     __syncwarp();
   } else {
     float* s32 = reinterpret_cast<float*>(st);
-    float* outp = static_cast<float*>(p.out);
+    float* outp = static_cast<float*>(p.out) + out_off;
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) s32[j * 32 + lane] = __uint_as_float(r[j]) + bias_v;
     __syncwarp();
@@ -458,6 +460,9 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
   const int cid = static_cast<int>(blockIdx.x >> 1), ncl = static_cast<int>(gridDim.x >> 1);
   const int npairs = p.num_w_tiles / 2;
   const int ntiles = p.num_x_tiles * npairs;
+  // work items: (pair tile, K range); with p.splits > 1 each item covers KT / p.splits K steps and writes an fp32
+  // partial that a reduction kernel adds up
+  const int nitems = ntiles * p.splits;
 
   auto stage_x = [&](int s) { return smem + C::kXOff + s * XH_BYTES; };
   auto stage_a = [&](int s) { return smem + C::kAOff + s * WE_BYTES; };
@@ -488,7 +493,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
   cluster_sync();  // both CTAs' barriers and TMEM exist before any signal crosses the pair
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const int KT = p.KT;
+  const int KT = p.KT, KTs = p.KT / p.splits;
 
   if (warp == 0) {
     // ---------------- producer: this CTA's activation half and weight tile ----------------
@@ -496,10 +501,11 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       int kiter = 0;
       uint32_t issued = 0, last_par = 0;
       bool ok = true;
-      for (int t = cid; ok && t < ntiles; t += ncl) {
-        const int xt = t % p.num_x_tiles, wt = 2 * (t / p.num_x_tiles) + static_cast<int>(rank);
+      for (int t = cid; ok && t < nitems; t += ncl) {
+        const int tt = t % ntiles, kt0 = (t / ntiles) * KTs;
+        const int xt = tt % p.num_x_tiles, wt = 2 * (tt / p.num_x_tiles) + static_cast<int>(rank);
         const uint8_t* wsrc = p.w9 + static_cast<int64_t>(wt) * KT * W9_BYTES;
-        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+        for (int kt = kt0; kt < kt0 + KTs; ++kt, ++kiter) {
           const int s = kiter % S;
           const uint32_t ph = (kiter / S) & 1;
           if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
@@ -521,12 +527,12 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       constexpr uint32_t idesc = idesc_bf16(2 * BM, BN);
       int kiter = 0, it = 0;
       bool ok = true, any = false;
-      for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
+      for (int t = cid; ok && t < nitems; t += ncl, ++it) {
         const int b = C::kAccBufs == 2 ? (it & 1) : 0, use = C::kAccBufs == 2 ? (it >> 1) : it;
         if (!mbar_wait_warp(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * 256;
-        for (int kt = 0; kt < KT; ++kt, ++kiter) {
+        for (int kt = 0; kt < KTs; ++kt, ++kiter) {   // kt: K step within the item (accumulate from its second)
           const int s = kiter % S;
           const uint32_t ph = (kiter / S) & 1;
           // both CTAs' expanders have decoded stage s, which they did after its loads landed
@@ -575,8 +581,8 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     const int grp = (e >> 2) / P;
     int kiter = 0;
     bool ok = true;
-    for (int t = cid; ok && t < ntiles; t += ncl) {
-      for (int kt = 0; kt < KT; ++kt, ++kiter) {
+    for (int t = cid; ok && t < nitems; t += ncl) {
+      for (int kt = 0; kt < KTs; ++kt, ++kiter) {
         if (G > 1 && (kiter % G) != grp) continue;
         const int s = kiter % S;
         const uint32_t ph = (kiter / S) & 1;
@@ -610,8 +616,10 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     constexpr int NC = BN / 2 / kChunk;
     int it = 0;
     bool ok = true;
-    for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
-      const int xt = t % p.num_x_tiles, wt = 2 * (t / p.num_x_tiles) + static_cast<int>(rank);
+    for (int t = cid; ok && t < nitems; t += ncl, ++it) {
+      const int tt = t % ntiles;
+      const int64_t out_off = static_cast<int64_t>(t / ntiles) * p.split_stride;
+      const int xt = tt % p.num_x_tiles, wt = 2 * (tt / p.num_x_tiles) + static_cast<int>(rank);
       const int b = C::kAccBufs == 2 ? (it & 1) : 0, use = C::kAccBufs == 2 ? (it >> 1) : it;
       float bias_v = 0.0f;
       if (p.bias) {
@@ -629,7 +637,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < NC; c += 2) {
         RL_TMEM_LD16(tbase + (c + 1) * kChunk, rb);
-        epilogue_chunk(p, ra, st, lane, q, wt, xb + c * kChunk, bias_v);
+        epilogue_chunk(p, ra, st, lane, q, wt, xb + c * kChunk, bias_v, out_off);
         tmem_ld_wait_regs(rb);
         if (c + 2 < NC) {
           RL_TMEM_LD16(tbase + (c + 2) * kChunk, ra);
@@ -638,7 +646,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(at_leader(&bars->acce[b]));
         }
-        epilogue_chunk(p, rb, st, lane, q, wt, xb + (c + 1) * kChunk, bias_v);
+        epilogue_chunk(p, rb, st, lane, q, wt, xb + (c + 1) * kChunk, bias_v, out_off);
         if (c + 2 < NC) tmem_ld_wait_regs(ra);
       }
     }
@@ -724,7 +732,7 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
     if (n <= 0) return fail(RL_ERR_UNSUPPORTED, "rl_linear_bfp16: no CTA pair fits on this device");
     max_clusters[dev] = n;
   }
-  const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2);
+  const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2) * p.splits;
   const int nclusters = ntiles < max_clusters[dev] ? ntiles : max_clusters[dev];
   cfg.gridDim = dim3(2 * nclusters);
   RL_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p));
@@ -766,10 +774,100 @@ int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) 
   return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
 }
 
+// Split-K for the pair kernel on a grid that would not fill the GPU: the largest S in {2, 4} with S x (pair tiles)
+// <= clusters (one pair of SMs each), KT % S == 0 and at least 16 K steps per split; 1 when no split helps.
+inline int choose_splits(int64_t M, int64_t K, int64_t N) {
+  if (N % 256) return 1;
+  const int64_t clusters = sm_count() / 2;
+  const int64_t tiles = (M + BN - 1) / BN * (N / 256);
+  const int64_t KT = K / BK;
+  int S = 1;
+  for (int c = 2; c <= 4; c *= 2)
+    if (tiles * c <= clusters && KT % c == 0 && KT / c >= 16) S = c;
+  return S;
+}
+
+// out[m][n] = sum over s of part[s][m][n] (+ bias[n]), to bf16 (round to nearest even) or fp32; 4 columns a thread.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int S, int64_t MN, int64_t N,
+                                                            const uint16_t* __restrict__ bias, void* __restrict__ out,
+                                                            int out_f32) {
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x) * 4; i < MN;
+       i += static_cast<int64_t>(gridDim.x) * 256 * 4) {
+    float4 a = *reinterpret_cast<const float4*>(part + i);
+    for (int sp = 1; sp < S; ++sp) {
+      const float4 b = *reinterpret_cast<const float4*>(part + sp * MN + i);
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    if (bias) {
+      const int64_t n = i % N;
+      a.x += bf16_bits_to_float(bias[n]);
+      a.y += bf16_bits_to_float(bias[n + 1]);
+      a.z += bf16_bits_to_float(bias[n + 2]);
+      a.w += bf16_bits_to_float(bias[n + 3]);
+    }
+    if (out_f32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = a;
+    } else {
+      const uint32_t lo = float_to_bf16_bits(a.x) | (float_to_bf16_bits(a.y) << 16);
+      const uint32_t hi = float_to_bf16_bits(a.z) | (float_to_bf16_bits(a.w) << 16);
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + i) = make_uint2(lo, hi);
+    }
+  }
+}
+
 }  // namespace gemm
 }  // namespace rl
 
 extern "C" {
+
+size_t rl_linear_bfp16_workspace(int64_t M, int64_t K, int64_t N, int epilogue) {
+  if (M <= 0 || K < 64 || K % 64 || N < 128 || N % 128 || epilogue == RL_EPI_SWIGLU) return 0;
+  const int S = rl::gemm::choose_splits(M, K, N);
+  return S > 1 ? static_cast<size_t>(S) * M * N * 4 : 0;
+}
+
+int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                       const uint16_t* bias, int epilogue, void* out, int out_dtype, void* workspace,
+                       size_t workspace_bytes, rl_stream_t stream) {
+  using namespace rl;
+  using namespace rl::gemm;
+  const size_t need = rl_linear_bfp16_workspace(M, K, N, epilogue);
+  if (need == 0 || g_variant != 0 || workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))
+    return rl_linear_bfp16(x, M, K, w_native, N, bias, epilogue, out, out_dtype, stream);
+  RL_REQUIRE(epilogue != RL_EPI_BIAS || bias != nullptr, RL_ERR_ARGUMENT, "rl_linear_bfp16: RL_EPI_BIAS needs bias");
+  RL_REQUIRE(out_dtype == RL_BF16 || out_dtype == RL_F32, RL_ERR_ARGUMENT, "rl_linear_bfp16: bad out dtype");
+  RL_REQUIRE(x && w_native && out, RL_ERR_ARGUMENT, "rl_linear_bfp16: NULL pointer");
+  RL_REQUIRE(aligned(x, 16) && aligned(w_native, 16) && aligned(out, 16), RL_ERR_ALIGNMENT,
+             "rl_linear_bfp16: x, w_native and out must be 16-byte aligned");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_linear_bfp16: needs an sm_100 device");
+  Params p;
+  p.w9 = w_native;
+  p.bias = nullptr;
+  p.out = workspace;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out_f32 = 1;
+  p.epilogue = RL_EPI_NONE;
+  p.num_x_tiles = static_cast<int>((M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(K / BK);
+  p.splits = choose_splits(M, K, N);
+  p.split_stride = M * N;
+  int st = launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
+  if (st != RL_OK) return st;
+  const int64_t MN = M * N;
+  const int64_t blocks = (MN / 4 + 255) / 256, cap = static_cast<int64_t>(sm_count()) * 8;
+  splitk_reduce_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, stream>>>(
+      static_cast<const float*>(workspace), p.splits, MN, N, epilogue == RL_EPI_BIAS ? bias : nullptr, out,
+      out_dtype == RL_F32 ? 1 : 0);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
 
 int rl_set_gemm_variant(int variant) {
   const int prev = rl::gemm::g_variant;
@@ -809,6 +907,8 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
   p.num_w_tiles = static_cast<int>(N / BM);
   p.num_tiles = p.num_x_tiles * p.num_w_tiles;
   p.KT = static_cast<int>(K / BK);
+  p.splits = 1;
+  p.split_stride = 0;
   return dispatch(g_variant, x, p, stream);
 }
 
@@ -822,9 +922,14 @@ namespace mlp {
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Workspace layout: [quantised x (M x K bf16) unless x is already bfp16-exact][H (M x F bf16)].
-inline size_t workspace_bytes(int64_t M, int64_t K, int64_t F, int x_quantized) {
+// Workspace layout: [quantised x (M x K bf16) unless x is already bfp16-exact][H (M x F bf16)][split-K partials of
+// the down GEMM, sized for N = K (the usual MLP), when the down GEMM's grid is small enough to split (optional: a
+// smaller workspace runs the down GEMM unsplit)].
+inline size_t base_bytes(int64_t M, int64_t K, int64_t F, int x_quantized) {
   return (x_quantized ? 0 : align256(static_cast<size_t>(M) * K * 2)) + align256(static_cast<size_t>(M) * F * 2);
+}
+inline size_t workspace_bytes(int64_t M, int64_t K, int64_t F, int x_quantized) {
+  return base_bytes(M, K, F, x_quantized) + align256(rl_linear_bfp16_workspace(M, F, K, RL_EPI_NONE));
 }
 
 int run(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up, int64_t F2,
@@ -835,8 +940,8 @@ int run(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const
              "swiglu_mlp: need K %% 64 == 0, 2F %% 256 == 0, N %% 128 == 0");
   RL_REQUIRE(!x_quantized || x_dtype == RL_BF16, RL_ERR_ARGUMENT, "swiglu_mlp: a quantised x must be bf16");
   const int64_t F = F2 / 2;
-  RL_REQUIRE(ws_bytes >= workspace_bytes(M, K, F, x_quantized), RL_ERR_ARGUMENT,
-             "swiglu_mlp: workspace of %zu bytes, need %zu", ws_bytes, workspace_bytes(M, K, F, x_quantized));
+  const size_t base = base_bytes(M, K, F, x_quantized);
+  RL_REQUIRE(ws_bytes >= base, RL_ERR_ARGUMENT, "swiglu_mlp: workspace of %zu bytes, need at least %zu", ws_bytes, base);
   RL_REQUIRE(aligned(ws, 256), RL_ERR_ALIGNMENT, "swiglu_mlp: workspace must be 256-byte aligned");
   if (M == 0) return RL_OK;
   const uint16_t* xq = static_cast<const uint16_t*>(x);
@@ -849,8 +954,8 @@ int run(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const
   }
   int st = rl_linear_bfp16(xq, M, K, w_up, F2, nullptr, RL_EPI_SWIGLU, h, RL_BF16, stream);
   if (st != RL_OK) return st;
-  return rl_linear_bfp16(reinterpret_cast<const uint16_t*>(h), M, F, w_down, N, nullptr, RL_EPI_NONE, out,
-                         out_dtype, stream);
+  return rl_linear_bfp16_ws(reinterpret_cast<const uint16_t*>(h), M, F, w_down, N, nullptr, RL_EPI_NONE, out,
+                            out_dtype, ws + base, ws_bytes - base, stream);
 }
 
 }  // namespace mlp
@@ -920,7 +1025,7 @@ int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M
                           rl_stream_t stream) {
   using namespace rl;
   RL_REQUIRE(M >= 0 && K > 0 && F2 > 0 && N > 0, RL_ERR_ARGUMENT, "rl_swiglu_mlp_noalloc: bad shape");
-  const size_t need = mlp::workspace_bytes(M, K, F2 / 2, x_quantized);
+  const size_t need = mlp::base_bytes(M, K, F2 / 2, x_quantized);   // the split-K partials are optional
   RL_REQUIRE(need <= mlp::kStaticScratchBytes, RL_ERR_ARGUMENT,
              "rl_swiglu_mlp_noalloc: M=%lld K=%lld F=%lld needs %zu bytes of scratch, more than the fixed %zu bytes "
              "(use rl_swiglu_mlp with a caller workspace)",

@@ -132,3 +132,36 @@ def test_swiglu_up(env, variant, M, K, F):
     assert err <= 2e-3, f"max-rel {err:.3e}: {_diag(got, href_q)}"
     # the same bfp16 values almost everywhere (blocks whose rounding sits on a tie can differ by one step)
     assert np.mean(got == href_q) > 0.99
+
+
+def test_linear_split_k_small_grid(env):
+    """rl_linear_bfp16_ws: 32 pair tiles with 96 K steps each run as 2 K ranges (fp32 partials in the workspace, then
+    a reduction adding them and the bias); matches the oracle on sampled rows and the unsplit kernel up to fp32
+    summation order, and a too-small workspace falls back to the unsplit kernel."""
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    M, K, N = 512, 6144, 4096
+    x, W, b = _case(M, K, N, seed=11)
+    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+    w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
+    bt = torch.from_numpy(b).to(dev).to(torch.bfloat16)
+    need = L.lib().rl_linear_bfp16_workspace(M, K, N, L.RL_EPI_BIAS)
+    assert need == 2 * M * N * 4
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    rows = np.r_[0:16, 500:512]
+    _, xd = O.quantize_rows(x[rows])
+    ref = O.linear(xd, O.unpack_b(O.pack_b(W), K, N), b)
+    for dt, code, tol, agree in ((torch.bfloat16, L.RL_BF16, BF16_OUT_TOL, 2.0 ** -7), (torch.float32, L.RL_F32, 2e-3, 1e-5)):
+        c = torch.empty((M, N), dtype=dt, device=dev)
+        L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
+               c.data_ptr(), code, ws.data_ptr(), need, s)
+        u = ops.linear_bfp16(dq, w, bias=bt, out_dtype=dt)
+        ops.device_status()
+        got = c.float().cpu().numpy()[rows]
+        assert O.max_rel(got, ref) <= tol, _diag(got, ref)
+        assert (c.float() - u.float()).abs().max().item() <= agree * u.float().abs().max().item()
+    c = torch.empty((M, N), dtype=torch.float32, device=dev)
+    L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
+           c.data_ptr(), L.RL_F32, ws.data_ptr(), need - 16, s)
+    assert torch.equal(c, ops.linear_bfp16(dq, w, bias=bt, out_dtype=torch.float32))
