@@ -334,23 +334,30 @@ def measure_configs(dev, stream, ws, seed):
     del model
     torch.cuda.empty_cache()
     out["next_rows"] = measure_next_rows(dev, stream, seed)
-    if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1 (NCCL all-reduce of bf16 partials)
+    if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1
         import torch.distributed as dist
         rank = dist.get_rank()
-        w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
-        tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD))
-        del w
-        torch.cuda.empty_cache()
         lat1 = torch.randn((cfg.image, cfg.latent_ch), generator=torch.Generator(device=dev).manual_seed(7),
                            device=dev)
         txt1 = torch.randn((cfg.text, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(8), device=dev)
-        dist.barrier()
-        ms = _event_ms(lambda: tp_model.denoise_step(lat1, txt1, 3), 3, 2, stream)
-        out[f"C4_dit_step_tp{ws}"] = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
-                                      "all_reduce_per_step": 2 * cfg.blocks, "all_reduce_bytes": cfg.M * cfg.hidden * 2,
-                                      "all_reduce_dtype": "bf16"}
-        del tp_model
-        torch.cuda.empty_cache()
+        # the default reduction (at 2 GPUs: the LayerNorm kernel sums the peers' bf16 partials over NVLink; else an
+        # NCCL all-reduce of the bf16 partials), and at 2 GPUs the NCCL all-reduce beside it
+        for mode in (["auto", "bf16"] if ws == 2 else ["auto"]):
+            w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
+            tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD),
+                               reduce_dtype=mode)
+            del w
+            torch.cuda.empty_cache()
+            dist.barrier()
+            ms = _event_ms(lambda: tp_model.denoise_step(lat1, txt1, 3), 3, 2, stream)
+            key = f"C4_dit_step_tp{ws}" + ("" if mode == "auto" else "_nccl_bf16")
+            out[key] = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
+                        "reductions_per_step": 2 * cfg.blocks, "partial_bytes": cfg.M * cfg.hidden * 2,
+                        "reduction": "peer reads in the LayerNorm kernel" if tp_model.reduce_dtype == "peer"
+                        else "NCCL all-reduce, bf16"}
+            tp_model.close()
+            del tp_model
+            torch.cuda.empty_cache()
     L.device_status()      # raises if any kernel recorded a device-side error
     return out
 

@@ -281,6 +281,32 @@ int rl_npu_kv_unpack(const uint8_t* kv_in, int H, int tiles_per_head, int tile0,
                      int64_t nk, int64_t ldv, uint16_t* k, uint16_t* vt, rl_stream_t stream);
 int rl_npu_qkv_tables(const uint16_t* tables, int T, float* rope_cs, float* w_q, float* w_k, rl_stream_t stream);
 
+/* Tensor-parallel residual + LayerNorm with the row-split projection's all-reduce fused in (the reference's TP plan:
+ * one all-reduce of the out- and down-projection partials per sublayer). Every rank's projection writes its bf16 (M, D)
+ * partial into a peer-readable buffer (rl_ipc_alloc); rl_tp_signal stores `epoch` into entry [slot][rank] of every rank's signal pad
+ * (pads: device array of W pointers to the pads' bases, each W x nslots uint64, zero before first use);
+ * rl_ln_mod_tp (rl_ln_mod's math with the branch = bf16 of the fp32 sum, in rank order, of the W partials `parts`, a
+ * device array of W pointers) first waits until this rank's pad (`pad` = its base + slot * W) holds >= epoch for
+ * every other rank - a bounded wait that records a device error when it runs out. Epochs increase by one per use of
+ * a slot; two slots used alternately keep a rank's next write of a partial after every rank's read of it. */
+/* Peer-readable device buffers for the fused reduction: rl_ipc_alloc returns a zeroed cudaMalloc allocation and its
+ * 64-byte CUDA IPC handle; the other ranks map it with rl_ipc_open (rl_ipc_close unmaps it, rl_ipc_free frees the
+ * owner's allocation). */
+int rl_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int rl_ipc_open(const void* handle, void** ptr);
+int rl_ipc_close(void* ptr);
+int rl_ipc_free(void* ptr);
+/* rl_linear_bfp16 with bf16 output (no SwiGLU) that also stores every output value at the same offset of `mirror`
+ * (a second M x N bf16 buffer, e.g. a peer GPU's mapping): the tensor-parallel projection sends its partial to the
+ * other rank while the GEMM runs. */
+int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                           const uint16_t* bias, int epilogue, void* out, void* mirror, int out_dtype,
+                           rl_stream_t stream);
+int rl_tp_signal(void* const* pads, int W, int rank, int slot, unsigned long long epoch, rl_stream_t stream);
+int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
+                 unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D, int64_t row_split,
+                 uint16_t* x_out, uint16_t* y_dq, uint8_t* y_q, rl_stream_t stream);
+
 /* GEMM kernel variant for tests and benchmarks: 0 = default (the 2-SM pair kernel with weights decoded into TMEM
  * when N is a multiple of 256, else variant 2), 1 = 1-SM, weights decoded into shared memory (MMA A operand from
  * shared memory), 2 = 1-SM, weights decoded into tensor memory (A from TMEM), 3 / 4 = 2-SM pair kernel

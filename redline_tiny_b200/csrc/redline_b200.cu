@@ -8,3 +8,4 @@
 #include "rl_conv.cu"
 #include "rl_adaln.cu"
 #include "rl_npu.cu"
+#include "rl_tp.cu"

@@ -78,6 +78,8 @@ struct Params {
   int num_x_tiles, num_w_tiles, num_tiles, KT;
   int splits;            // pair kernel: K split into this many ranges, fp32 partials split_stride elements apart
   int64_t split_stride;
+  void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
+                           // a peer GPU's buffer for the tensor-parallel reduction)
 };
 
 struct Barriers {
@@ -141,6 +143,23 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
       if (xr < p.M)
         *reinterpret_cast<uint4*>(outp + xr * p.N + static_cast<int64_t>(wt) * BM + 32 * q + part * 8) =
             reinterpret_cast<const uint4*>(s16 + rr * 32)[part];
+    }
+    if (p.mirror) {
+      // the staged chunk again into the mirror (a peer GPU's buffer): one 64-byte bulk copy per row, so the
+      // copy engine of the SM carries the NVLink stores and the warp waits only until the chunk has been read
+      // (addresses: staging rows 64 bytes apart in a 16-byte aligned buffer; global rows start at column
+      // wt * 128 + 32 q of a row of N % 128 == 0 bf16 values - all 64-byte aligned)
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane < 16) {
+        const int64_t xr = x0 + lane;
+        if (xr < p.M) {
+          bulk_store(static_cast<uint16_t*>(p.mirror) + xr * p.N + static_cast<int64_t>(wt) * BM + 32 * q,
+                     s16 + lane * 32, 64);
+          bulk_commit();
+          bulk_store_wait_read();
+        }
+      }
     }
     __syncwarp();
   } else {
@@ -877,9 +896,17 @@ int rl_set_gemm_variant(int variant) {
 
 int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                     const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream) {
+  return rl_linear_bfp16_mirror(x, M, K, w_native, N, bias, epilogue, out, nullptr, out_dtype, stream);
+}
+
+int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                           const uint16_t* bias, int epilogue, void* out, void* mirror, int out_dtype,
+                           rl_stream_t stream) {
   using namespace rl;
   using namespace rl::gemm;
   RL_REQUIRE(x && w_native && out, RL_ERR_ARGUMENT, "rl_linear_bfp16: NULL pointer");
+  RL_REQUIRE(!mirror || (out_dtype == RL_BF16 && epilogue != RL_EPI_SWIGLU && aligned(mirror, 16)), RL_ERR_ARGUMENT,
+             "rl_linear_bfp16_mirror: the mirror needs a 16-byte aligned bf16 output without SwiGLU");
   RL_REQUIRE(M >= 0 && K >= 64 && K % 64 == 0 && N >= 128 && N % 128 == 0, RL_ERR_ARGUMENT,
              "rl_linear_bfp16: need K %% 64 == 0, N %% 128 == 0 (M=%lld K=%lld N=%lld)", (long long)M, (long long)K,
              (long long)N);
@@ -909,6 +936,7 @@ int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_na
   p.KT = static_cast<int>(K / BK);
   p.splits = 1;
   p.split_stride = 0;
+  p.mirror = mirror;
   return dispatch(g_variant, x, p, stream);
 }
 

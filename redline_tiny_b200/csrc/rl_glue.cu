@@ -38,9 +38,25 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 
 // One warp per row; lane l owns the 8-value blocks kb = l, l + 32, ... of the row.
 // params: bf16 [2][2][D] = {row 0: [g | sc], row 1: [g | sc]}; rows < row_split use row 1 (run_ln.py:82-86).
-__device__ __forceinline__ void load_branch(const void* br, int br_f32, int64_t r, int64_t D, int64_t kb,
+// The branch of a tensor-parallel row-split projection: the sum of the W ranks' bf16 partial outputs, each read from
+// its rank's memory (this process's mapping of it; peers over NVLink), added in rank order in fp32 so that every
+// rank forms the same value.
+struct TpBranch {
+  const uint16_t* const* parts;   // device array of W pointers, or null
+  int W;
+};
+
+__device__ __forceinline__ void load_branch(const void* br, int br_f32, TpBranch tp, int64_t r, int64_t D, int64_t kb,
                                             float (&f)[8]) {
-  if (!br) {
+  if (tp.W > 0) {
+    unpack8(*(reinterpret_cast<const uint4*>(tp.parts[0] + r * D) + kb), f);
+    for (int w = 1; w < tp.W; ++w) {
+      float g[8];
+      unpack8(*(reinterpret_cast<const uint4*>(tp.parts[w] + r * D) + kb), g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] += g[i];
+    }
+  } else if (!br) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) f[i] = 0.0f;
   } else if (br_f32) {
@@ -54,14 +70,44 @@ __device__ __forceinline__ void load_branch(const void* br, int br_f32, int64_t 
 
 // The branch is bf16, or fp32 (the sum of tensor-parallel partial GEMM outputs), rounded to bf16 on load in both
 // cases: x' = bf16(x + g * bf16(branch)).
+// tp.W > 0: the branch is the TP sum (TpBranch); the kernel first waits until every other rank has signalled that its
+// partial is complete (pad[r] >= epoch in this rank's signal pad, written by rl_tp_signal), a bounded wait that
+// records kErrWaitTimeout and returns when it runs out.
 __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __restrict__ x,
-                                                          const void* __restrict__ br, int br_f32,
+                                                          const void* __restrict__ br, int br_f32, TpBranch tp,
+                                                          const unsigned long long* pad, int rank,
+                                                          unsigned long long epoch,
                                                           const uint16_t* __restrict__ params, int64_t M, int64_t D,
                                                           int64_t row_split, float eps, int rms,
                                                           uint16_t* __restrict__ xo, uint16_t* __restrict__ y_dq,
                                                           uint8_t* __restrict__ y_q) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t KB = D >> 3;
+  if (tp.W > 0) {
+    __shared__ int ready;
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      for (int w = 0; ok && w < tp.W; ++w) {
+        if (w == rank) continue;
+        const long long t0 = clock64();
+        while (true) {
+          unsigned long long v;
+          asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pad + w) : "memory");
+          if (v >= epoch) break;
+          if (clock64() - t0 > RL_WAIT_LIMIT_CYCLES) {
+            report(kErrWaitTimeout);
+            ok = 0;
+            break;
+          }
+          __nanosleep(200);
+        }
+      }
+      ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
+    br_f32 = 1;   // the fp32 sum is rounded to bf16 like an fp32 branch
+  }
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < M; r += static_cast<int64_t>(gridDim.x) * kWarps) {
     const uint16_t* prow = params + (r < row_split ? 2 * D : 0);
     const uint16_t* g = prow;
@@ -72,7 +118,7 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
       float xf[8], bf[8], gf[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
       unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
-      load_branch(br, br_f32, r, D, kb, bf);
+      load_branch(br, br_f32, tp, r, D, kb, bf);
       if (br_f32) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
@@ -103,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
         float xf[8], bf[8], gf[8];
         unpack8(__ldg(reinterpret_cast<const uint4*>(x + r * D) + kb), xf);
         unpack8(__ldg(reinterpret_cast<const uint4*>(g) + kb), gf);
-        load_branch(br, br_f32, r, D, kb, bf);
+        load_branch(br, br_f32, tp, r, D, kb, bf);
         if (br_f32) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) bf[i] = bf16_bits_to_float(float_to_bf16_bits(bf[i]));
@@ -250,7 +296,8 @@ static int norm_mod(const char* fn, int rms, const uint16_t* x, const void* bran
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "%s: needs an sm_100 device", fn);
   if (M == 0) return RL_OK;
   glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      x, branch, branch_dtype == RL_F32 ? 1 : 0, params, M, D, row_split, 1e-6f, rms, x_out, y_dq, y_q);
+      x, branch, branch_dtype == RL_F32 ? 1 : 0, glue::TpBranch{nullptr, 0}, nullptr, 0, 0ull, params, M, D, row_split,
+      1e-6f, rms, x_out, y_dq, y_q);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

@@ -110,13 +110,19 @@ class DiT:
     """Resident packed weights + preallocated activations for one denoise step of config `cfg` on one GPU.
 
     tp = (rank, world, group): tensor-parallel over `world` GPUs with `weights` already sharded by shard_weights;
-    the out-projection and down-projection write partial sums that one NCCL all-reduce each adds up (two per block,
-    the block being two sequential sublayers), and the residual / LayerNorm run replicated. reduce_dtype: "bf16"
-    (default; the partials are rounded to bf16 before the sum, half the bytes on NVLink) or "fp32"."""
+    the out-projection and down-projection write partial sums that are added up across the group (two reductions per
+    block, the block being two sequential sublayers), and the residual / LayerNorm run replicated. reduce_dtype:
+    "peer" (2 GPUs: the projection GEMM stores its bf16 partial into the other rank's memory as it computes it and
+    the LayerNorm kernel adds the two: tp.PeerReduce), "bf16"
+    (one NCCL all-reduce of the bf16 partials), "fp32" (NCCL, fp32 partials) or "auto" (default: "peer" at 2 GPUs,
+    where the transfer overlaps the GEMM, "bf16" otherwise)."""
 
-    def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="bf16"):
-        if reduce_dtype not in ("bf16", "fp32"):
-            raise ValueError(f"reduce_dtype must be 'bf16' or 'fp32', not {reduce_dtype!r}")
+    def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto"):
+        if reduce_dtype not in ("auto", "peer", "bf16", "fp32"):
+            raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'bf16' or 'fp32', not {reduce_dtype!r}")
+        if reduce_dtype == "auto":
+            reduce_dtype = "peer" if tp and tp[1] == 2 else "bf16"
+        self.reduce_dtype = reduce_dtype if tp else None
         self.reduce_f32 = reduce_dtype == "fp32"
         self.cfg = cfg
         dev = torch.device(device)
@@ -181,6 +187,10 @@ class DiT:
         self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
         self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
         self.params = {k: torch.empty(2, 2, D, **bf) for k in ("first", "mlp", "attn", "out")}
+        self.peer = None
+        if tp and reduce_dtype == "peer":
+            from . import tp as TP
+            self.peer = TP.PeerReduce(tp[2], tp[0], tp[1], M, D, dev)
 
     # --- per-step adaLN parameters (forward.py:231-238), computed on the GPU ---
     def set_t(self, sigma):
@@ -206,7 +216,8 @@ class DiT:
 
     def _linear(self, x, w, out, epi=L.RL_EPI_NONE, out_dtype=L.RL_BF16):
         M, K = x.shape
-        L.call("rl_linear_bfp16", x.data_ptr(), M, K, w.native.data_ptr(), w.N, None, epi, out.data_ptr(), out_dtype,
+        dst = out if isinstance(out, int) else out.data_ptr()
+        L.call("rl_linear_bfp16", x.data_ptr(), M, K, w.native.data_ptr(), w.N, None, epi, dst, out_dtype,
                torch.cuda.current_stream().cuda_stream)
 
     def _ln(self, x, br, params, xo, y):
@@ -226,6 +237,30 @@ class DiT:
         self._linear(self.lat_dq, self.img_in, self.emb[cfg.text:])
         self.emb[:cfg.text].copy_(text_states.to(self.dev, torch.bfloat16))
         self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
+
+    def _branch_ln(self, x, w, xin, params, xo):
+        """The out / down projection followed by the residual + LayerNorm; under tensor parallelism the partial
+        projections are summed across the group first (in the LayerNorm kernel itself for reduce_dtype "peer")."""
+        if self.peer is None:
+            self._ln(xin, self._branch(x, w), params, xo, self.a)
+            return
+        s = torch.cuda.current_stream().cuda_stream
+        slot, epoch = self.peer.next()
+        out, mirror = self.peer.part(slot)
+        M, K = x.shape
+        L.call("rl_linear_bfp16_mirror", x.data_ptr(), M, K, w.native.data_ptr(), w.N, None, L.RL_EPI_NONE, out,
+               mirror, L.RL_BF16, s)
+        self.peer.signal(slot, epoch, s)
+        self.peer.ln_mod(xin, slot, epoch, params, self.cfg.text, xo, self.a, s)
+
+    def close(self):
+        """Release the peer buffers of reduce_dtype "peer" (a collective: every rank of the group calls it)."""
+        if self.peer is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.dev)
+            dist.barrier(group=self.tp[2])
+            self.peer.close()
+            self.peer = None
 
     def _branch(self, x, w):
         """The out / down projection: bf16 on one GPU; partial sums all-reduced across the TP group."""
@@ -250,11 +285,9 @@ class DiT:
                M, H, self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
         L.call("rl_attention", self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, H, M, M, M, None,
                1.0, self.o.data_ptr(), H * HEAD_DIM, s)
-        c = self._branch(self.o, b["o"])
-        self._ln(self.x[0], c, self.params["mlp"], self.x[1], self.a)
+        self._branch_ln(self.o, b["o"], self.x[0], self.params["mlp"], self.x[1])
         self._linear(self.a, b["up"], self.h, epi=L.RL_EPI_SWIGLU)
-        c = self._branch(self.h, b["down"])
-        self._ln(self.x[1], c, self.params["out" if last else "attn"], self.x[0], self.a)
+        self._branch_ln(self.h, b["down"], self.x[1], self.params["out" if last else "attn"], self.x[0])
 
     def project(self):
         """proj_out on the image rows of a (= norm_out output) -> velocity (image, 64) float32 (forward.py:261-269)."""

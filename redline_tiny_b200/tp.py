@@ -1,0 +1,99 @@
+"""Peer-memory reduction for the 2-GPU tensor-parallel DiT: the all-reduce of the out- and down-projection partials
+fused into the projection GEMM (which stores its partial into the other rank's memory as it computes it) and the
+residual + LayerNorm kernel (which adds the two partials: rl_ln_mod_tp).
+
+The reference's tensor-parallel plan sums the row-split projections' partial outputs across ranks before each
+residual + LayerNorm (one all-reduce per sublayer, two per block). Here each rank's projection GEMM writes its bf16
+partial tile by tile both into its own buffer and, over NVLink, into the other rank's (rl_linear_bfp16_mirror; the
+buffers are cudaMalloc allocations shared by CUDA IPC handle, plain peer stores), so the transfer overlaps the GEMM's
+math. A one-thread kernel then stores an epoch number into the other rank's signal pad; the LayerNorm kernel waits
+for the other rank's epoch (a bounded wait) and reads both partials from local memory. Each rank sends its partial
+once - the bytes a ring all-reduce moves - and no separate collective kernel runs.
+
+The sum is formed in fp32 in rank order and rounded to bf16 before the residual: this equals NCCL's bf16 sum of the
+two partials bit for bit.
+
+Buffer layout (per rank, one allocation): [slot 0: partial of rank 0 | of rank 1 | slot 1: same | pads: 2 slots x W
+uint64], partials M x D bf16. The out- and down-projections alternate between the slots; epochs increase by one per
+use. A rank stores into a slot again only after its wait on the other slot has passed, which the other rank signals
+after its LayerNorm finished reading the slot. Epochs are kernel arguments, so a CUDA graph of a step would replay
+stale epochs: this path is for eager launches only.
+"""
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+_ALIGN = 256
+
+
+class PeerReduce:
+    """The peer buffers of one tensor-parallel group: this rank's allocation and its mappings of the others'."""
+
+    def __init__(self, group, rank, world, M, D, device):
+        import torch.distributed as dist
+        if world != 2:
+            raise ValueError(f"the peer reduction is built for 2 ranks, not {world}")
+        self.rank, self.world, self.M, self.D = rank, world, M, D
+        self.part_bytes = (M * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.slot_bytes = world * self.part_bytes
+        self.pad_off = 2 * self.slot_bytes
+        total = self.pad_off + (2 * world * 8 + _ALIGN - 1) // _ALIGN * _ALIGN
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        L.call("rl_ipc_alloc", total, ctypes.byref(ptr), handle)
+        self.base = ptr.value
+        self.opened = []
+        try:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            bases = []
+            for w, h in enumerate(handles):
+                if w == rank:
+                    bases.append(self.base)
+                    continue
+                p = ctypes.c_void_p()
+                L.call("rl_ipc_open", (ctypes.c_char * 64).from_buffer_copy(h), ctypes.byref(p))
+                self.opened.append(p.value)
+                bases.append(p.value)
+        except Exception:
+            self.close()
+            raise
+        i64 = dict(dtype=torch.int64, device=device)
+        self.peer_base = bases[1 - rank]
+        self.parts = [torch.tensor([self.base + s * self.slot_bytes + w * self.part_bytes for w in range(world)], **i64)
+                      for s in range(2)]
+        self.pads = torch.tensor([b + self.pad_off for b in bases], **i64)
+        self.epoch = 0
+        self.group = group
+        dist.barrier(group=group)       # every rank's pads are zero and mapped before the first signal
+
+    def part(self, slot):
+        """(this rank's partial of `slot` here, its copy in the other rank's buffer): where the projection GEMM
+        stores its output."""
+        off = slot * self.slot_bytes + self.rank * self.part_bytes
+        return self.base + off, self.peer_base + off
+
+    def next(self):
+        """The (slot, epoch) of the next reduction."""
+        self.epoch += 1
+        return self.epoch & 1, self.epoch
+
+    def signal(self, slot, epoch, stream):
+        L.call("rl_tp_signal", self.pads.data_ptr(), self.world, self.rank, slot, epoch, stream)
+
+    def ln_mod(self, x, slot, epoch, params, row_split, x_out, y, stream):
+        """x_out = x + g * bf16(sum of the W partials of `slot`); y = LN(x_out) * scale as bfp16 values (bf16)."""
+        pad = self.base + self.pad_off + slot * self.world * 8
+        L.call("rl_ln_mod_tp", x.data_ptr(), self.parts[slot].data_ptr(), self.world, pad, self.rank, epoch,
+               params.data_ptr(), self.M, self.D, row_split, x_out.data_ptr(), y.data_ptr(), None, stream)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's; call after a barrier that follows the last use."""
+        for p in self.opened:
+            L.call("rl_ipc_close", p)
+        self.opened = []
+        if self.base:
+            L.call("rl_ipc_free", self.base)
+            self.base = 0

@@ -165,3 +165,26 @@ def test_linear_split_k_small_grid(env):
     L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
            c.data_ptr(), L.RL_F32, ws.data_ptr(), need - 16, s)
     assert torch.equal(c, ops.linear_bfp16(dq, w, bias=bt, out_dtype=torch.float32))
+
+
+@pytest.mark.parametrize("N", [3072, 384])   # the pair kernel and the 1-SM kernel
+def test_linear_mirror_stores_identical_copy(env, N):
+    """rl_linear_bfp16_mirror: the output and its mirror (here a second local buffer) both equal rl_linear_bfp16's
+    output bit for bit, ragged M included; a mirror with fp32 output or SwiGLU is refused."""
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    M, K = 300, 1536
+    x, W, b = _case(M, K, N, seed=12)
+    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+    w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
+    s = torch.cuda.current_stream().cuda_stream
+    out = torch.full((M, N), 3.0, dtype=torch.bfloat16, device=dev)
+    mir = torch.full((M, N), 5.0, dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16_mirror", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE, out.data_ptr(),
+           mir.data_ptr(), L.RL_BF16, s)
+    ref = ops.linear_bfp16(dq, w)
+    ops.device_status()
+    assert torch.equal(out, ref) and torch.equal(mir, ref)
+    with pytest.raises(L.RedlineError):
+        L.call("rl_linear_bfp16_mirror", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE,
+               out.data_ptr(), mir.data_ptr(), L.RL_F32, s)
