@@ -281,8 +281,8 @@ int rl_npu_kv_unpack(const uint8_t* kv_in, int H, int tiles_per_head, int tile0,
                      int64_t nk, int64_t ldv, uint16_t* k, uint16_t* vt, rl_stream_t stream);
 int rl_npu_qkv_tables(const uint16_t* tables, int T, float* rope_cs, float* w_q, float* w_k, rl_stream_t stream);
 
-/* Tensor-parallel residual + LayerNorm with the row-split projection's all-reduce fused in (the reference's TP plan:
- * one all-reduce of the out- and down-projection partials per sublayer). Every rank's projection writes its bf16 (M, D)
+/* Tensor-parallel residual + LayerNorm with the row-split projection's all-reduce fused in (the reference runs on one
+ * device; the TP DiT adds the out- and down-projection partials across ranks once per sublayer). Every rank's projection writes its bf16 (M, D)
  * partial into a peer-readable buffer (rl_ipc_alloc); rl_tp_signal stores `epoch` into entry [slot][rank] of every rank's signal pad
  * (pads: device array of W pointers to the pads' bases, each W x nslots uint64, zero before first use);
  * rl_ln_mod_tp (rl_ln_mod's math with the branch = bf16 of the fp32 sum, in rank order, of the W partials `parts`, a

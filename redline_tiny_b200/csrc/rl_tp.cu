@@ -1,7 +1,8 @@
 // Tensor-parallel reduction of the DiT's row-split projections, fused into the projection GEMM and the residual +
 // LayerNorm kernel.
 //
-// The reference's tensor-parallel plan (one all-reduce of the out- and down-projection partials per sublayer) needs
+// The reference runs on one device; this library's tensor-parallel DiT (one reduction of the out- and
+// down-projection partials per sublayer) needs
 // every rank to form bf16(sum of the W partials) before the residual and LayerNorm. Here each rank's projection GEMM
 // stores its bf16 partial, tile by tile as it is computed, into its own buffer and into the other rank's
 // (rl_linear_bfp16_mirror over a CUDA IPC peer mapping), so the NVLink transfer overlaps the GEMM's math;

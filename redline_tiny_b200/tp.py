@@ -2,8 +2,8 @@
 fused into the projection GEMM (which stores its partial into the other rank's memory as it computes it) and the
 residual + LayerNorm kernel (which adds the two partials: rl_ln_mod_tp).
 
-The reference's tensor-parallel plan sums the row-split projections' partial outputs across ranks before each
-residual + LayerNorm (one all-reduce per sublayer, two per block). Here each rank's projection GEMM writes its bf16
+The tensor-parallel DiT (the reference itself runs on one device) sums the row-split projections' partial outputs
+across ranks before each residual + LayerNorm (one reduction per sublayer, two per block). Here each rank's projection GEMM writes its bf16
 partial tile by tile both into its own buffer and, over NVLink, into the other rank's (rl_linear_bfp16_mirror; the
 buffers are cudaMalloc allocations shared by CUDA IPC handle, plain peer stores), so the transfer overlaps the GEMM's
 math. A one-thread kernel then stores an epoch number into the other rank's signal pad; the LayerNorm kernel waits
