@@ -67,3 +67,13 @@ def test_shard_shapes():
         assert s["gate"].shape == (12288 // world, 3072) and s["down"].shape == (12288 // world, 3072)
     with pytest.raises(AssertionError):
         dit.shard_weights(w, cfg, 0, 5)
+
+
+def test_reduction_choice_is_checked():
+    """DiT's reduce_dtype is checked before anything is allocated; the peer reduction is built for exactly 2 ranks."""
+    import pytest
+    from redline_tiny_b200 import dit, tp
+    with pytest.raises(ValueError, match="reduce_dtype"):
+        dit.DiT(dit.DiTConfig(blocks=1), {}, device="cpu", reduce_dtype="fp16")
+    with pytest.raises(ValueError, match="2 ranks"):
+        tp.PeerReduce(None, 0, 4, 64, 256, "cpu")
