@@ -211,7 +211,7 @@ def _event_ms(fn, n, w, stream):
 def measure_next_rows(dev, stream, seed):
     """The paths beyond configs 1-5 (CUDA events, seeded synthetic inputs, random N(0, 0.02) weights): the VAE
     decoder's 3x3 convolutions at two of its stages (vae_decode.py:311-348: 1152 channels at 128^2, 288 at 512^2 -
-    K = 9 * 288 padded to 2624) and one Qwen3-VL-8B decoder layer at the reference's M = 1536 rows (vlm_run.py:396-431,
+    K = 9 taps x 288 channels, each padded to 320) and one Qwen3-VL-8B decoder layer at the reference's M = 1536 rows (vlm_run.py:396-431,
     causal GQA over 1500 valid rows)."""
     import math
     import torch
@@ -228,7 +228,9 @@ def measure_next_rows(dev, stream, seed):
         ms = _event_ms(lambda: ops.conv2d(x, pw, bias, taps, out=y), 10, 3, stream)
         fl = 2.0 * H * H * 9 * C * C
         res[f"vae_conv3_{H}x{H}x{C}"] = {"ms": ms, "TFLOP/s": fl / (ms * 1e-3) / 1e12, "GFLOP": fl / 1e9,
-                                         "gather_bytes": H * H * ops.conv_k(C, 3) * 2}
+                                         "gather_bytes": L.lib().rl_conv2d_workspace(H, H, C, 3),
+                                         "path": "implicit GEMM (3-D TMA from the image)"
+                                         if L.lib().rl_conv2d_workspace(H, H, C, 3) == 0 else "im2col + GEMM"}
         del x, w, pw, y
     cfg = vlm.LMConfig()
     M, valid = 1536, 1500

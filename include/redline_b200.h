@@ -237,12 +237,16 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
  * artifacts (kernels/vae/vconv.cc:1-17, redline/vae_decode.py:168-194; weights packed by vae_ops.pack_vconv,
  * vae_ops.py:44-61) and is checked against vae_ops.conv_ref (vae_ops.py:64-75).
  * x: (H, W, Cin) bf16 holding bfp16-exact values (rl_quantize_bfp16's decoded output of the (H * W, Cin) matrix);
- * Cin % 8 == 0. w_native: the native tiles of B = [(dy * taps + dx) * Cin + ci][co] = w[co][ci][dy][dx] with zero rows
- * after the last tap up to K = taps^2 * Cin rounded up to a multiple of 64; N = Cout, a multiple of 128 (pad smaller
- * outputs with zero columns); bias: bf16 [Cout] or NULL; out: (H, W, Cout) bf16. workspace:
- * rl_conv2d_workspace(H, W, Cin, taps) bytes (the gathered rows of K columns; 0 for a 1x1 conv with Cin % 64 == 0).
+ * Cin % 8 == 0. w_native: the native tiles of B = [(dy * taps + dx) * Kt + ci][co] = w[co][ci][dy][dx], Kt = Cin
+ * rounded up to a multiple of 64 (zero rows for Cin <= ci < Kt), K = taps^2 * Kt; N = Cout, a multiple of 128 (pad
+ * smaller outputs with zero columns); bias: bf16 [Cout] or NULL; out: (H, W, Cout) bf16. With W % 128 == 0 and
+ * Cin >= 64 the GEMM loads its A tiles from x directly (implicit GEMM, TMA zero fill as the padding) and needs no
+ * workspace; otherwise the rows are gathered first into the workspace: rl_conv2d_workspace(H, W, Cin, taps) bytes
+ * (0 when nothing is gathered: the implicit GEMM, or a 1x1 conv with Cin % 64 == 0).
+ * rl_set_conv_path(1) forces the gather for every shape (0: the default choice); it returns the previous setting.
  */
 size_t rl_conv2d_workspace(int H, int W, int Cin, int taps);
+int rl_set_conv_path(int path);
 int rl_conv2d_bfp16(const uint16_t* x, int H, int W, int Cin, const uint8_t* w_native, int Cout, int taps,
                     const uint16_t* bias, uint16_t* out, void* workspace, size_t workspace_bytes,
                     rl_stream_t stream);

@@ -35,6 +35,7 @@ SIGNATURES = {
     "rl_linear_bfp16_ws": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P, ctypes.c_size_t, _P]),
     "rl_set_gemm_variant": (_I, [_I]),
     "rl_set_attention_variant": (_I, [_I]),
+    "rl_set_conv_path": (_I, [_I]),
     "rl_conv2d_workspace": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "rl_conv2d_bfp16": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),
     "rl_swiglu_mlp_workspace": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),

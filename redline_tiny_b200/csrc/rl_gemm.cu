@@ -80,7 +80,23 @@ struct Params {
   int64_t split_stride;
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
+  // Convolution (implicit GEMM) when conv_W > 0: the A rows are the pixels of an (H, W, C) image (W % 128 == 0), the
+  // tensor map is 3-D over (C, W, H), and K step kt covers channels 64 (kt % conv_cpt) .. + 63 of tap kt / conv_cpt
+  // (taps in (dy, dx) row-major order, conv_cpt = ceil(C / 64) steps per tap).
+  int conv_W = 0, conv_H = 0, conv_C = 0, conv_taps = 0, conv_cpt = 0;
 };
+
+// Conv mode: the 128 A rows starting at pixel pix0 (one image row, since W % 128 == 0) for K step kt, read from the
+// image at the tap's offset; TMA's zero fill outside the (C, W, H) box is the convolution's zero padding (the
+// innermost coordinate is a multiple of 64 channels and never negative; the others may be -1 or W / H).
+__device__ __forceinline__ void load_conv_rows(void* dst, const CUtensorMap* map, uint64_t* bar, const Params& p,
+                                               int kt, int pix0) {
+  const int tap = kt / p.conv_cpt, cb = kt - tap * p.conv_cpt;
+  const int half = p.conv_taps >> 1;
+  const int dy = tap / p.conv_taps - half, dx = tap % p.conv_taps - half;
+  const int h = pix0 / p.conv_W, w = pix0 - h * p.conv_W;
+  tma_load_3d(dst, map, bar, cb * BK, w + dx, h + dy);
+}
 
 struct Barriers {
   uint64_t full[8];      // producer tx: X + W9 landed
@@ -273,7 +289,12 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
           const uint32_t ph = (kiter / C::kStages) & 1;
           if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->full[s], X_BYTES + W9_BYTES);
-          tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN);
+          if (p.conv_W) {   // two 128-pixel runs make the 256-row tile (the second lands 128 rows = 16 KB later)
+            load_conv_rows(stage_x(s), &tmap_x, &bars->full[s], p, kt, xt * BN);
+            load_conv_rows(stage_x(s) + 128 * 128, &tmap_x, &bars->full[s], p, kt, xt * BN + 128);
+          } else {
+            tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN);
+          }
           bulk_load(stage_w9(s), wsrc + static_cast<int64_t>(kt) * W9_BYTES, W9_BYTES, &bars->full[s]);
           issued |= 1u << s;
           last_par = (last_par & ~(1u << s)) | (ph << s);
@@ -529,7 +550,10 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
           const uint32_t ph = (kiter / S) & 1;
           if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->full[s], XH_BYTES + W9_BYTES);
-          tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN + static_cast<int>(rank) * 128);
+          if (p.conv_W)
+            load_conv_rows(stage_x(s), &tmap_x, &bars->full[s], p, kt, xt * BN + static_cast<int>(rank) * 128);
+          else
+            tma_load_2d(stage_x(s), &tmap_x, &bars->full[s], kt * BK, xt * BN + static_cast<int>(rank) * 128);
           bulk_load(stage_w9(s), wsrc + static_cast<int64_t>(kt) * W9_BYTES, W9_BYTES, &bars->full[s]);
           issued |= 1u << s;
           last_par = (last_par & ~(1u << s)) | (ph << s);
@@ -699,11 +723,30 @@ inline int make_x_map(CUtensorMap* map, const uint16_t* x, int64_t M, int64_t K,
   return RL_OK;
 }
 
+// The A operand's map: 2-D (K, M) with `box_rows` rows, or in conv mode the 3-D map over the (H, W, C) image
+// (box = 64 channels x 128 pixels x 1 row; out-of-range elements read as zero).
+inline int make_a_map(CUtensorMap* map, const uint16_t* x, const Params& p, int box_rows) {
+  if (!p.conv_W) return make_x_map(map, x, p.M, p.K, box_rows);
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(RL_ERR_CUDA, "rl_conv2d_bfp16: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t gdim[3] = {static_cast<cuuint64_t>(p.conv_C), static_cast<cuuint64_t>(p.conv_W),
+                              static_cast<cuuint64_t>(p.conv_H)};
+  const cuuint64_t gstride[2] = {static_cast<cuuint64_t>(p.conv_C) * 2,
+                                 static_cast<cuuint64_t>(p.conv_C) * 2 * static_cast<cuuint64_t>(p.conv_W)};
+  const cuuint32_t box[3] = {BK, 128, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult cr = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(x), gdim, gstride, box,
+                          estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(RL_ERR_CUDA, "rl_conv2d_bfp16: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+  return RL_OK;
+}
+
 template <int V, int S, int G, int P>
 int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
   using C = Cfg<V, S, G, P>;
   CUtensorMap tmap;
-  int st = make_x_map(&tmap, x, p.M, p.K, BN);
+  int st = make_a_map(&tmap, x, p, BN);
   if (st != RL_OK) return st;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -726,7 +769,7 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   using C = pair::Cfg<V, S, G, P>;
   auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P>;
   CUtensorMap tmap;
-  int st = make_x_map(&tmap, x, p.M, p.K, 128);
+  int st = make_a_map(&tmap, x, p, 128);
   if (st != RL_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -941,6 +984,45 @@ int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------
+// Convolution as an implicit GEMM: the A tile of each K step is loaded straight from the (H, W, C) image.
+// ------------------------------------------------------------------------------------------------------------
+namespace rl {
+namespace gemm {
+
+// out (H * W, N) = conv(x (H, W, C), w) with the weight packed as B = [(dy, dx, c padded to cpt * 64)][N]; needs
+// W % 128 == 0 (a 128-pixel A run stays in one image row), C % 8 == 0 and C >= 64 (the 64-channel box never exceeds
+// the channel extent as a whole).
+int linear_conv(const uint16_t* x, int H, int W, int C, int taps, const uint8_t* w_native, int64_t N,
+                const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
+  RL_REQUIRE(W % 128 == 0 && C % 8 == 0 && C >= 64 && (taps == 1 || taps == 3), RL_ERR_ARGUMENT,
+             "conv: implicit GEMM needs W %% 128 == 0, C %% 8 == 0, C >= 64");
+  Params p;
+  p.w9 = w_native;
+  p.bias = bias;
+  p.out = out;
+  p.M = static_cast<int64_t>(H) * W;
+  p.N = N;
+  p.conv_cpt = (C + BK - 1) / BK;
+  p.K = static_cast<int64_t>(taps) * taps * p.conv_cpt * BK;
+  p.out_f32 = 0;
+  p.epilogue = bias ? RL_EPI_BIAS : RL_EPI_NONE;
+  p.num_x_tiles = static_cast<int>((p.M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(p.K / BK);
+  p.splits = 1;
+  p.split_stride = 0;
+  p.conv_W = W;
+  p.conv_H = H;
+  p.conv_C = C;
+  p.conv_taps = taps;
+  return dispatch(g_variant, x, p, stream);
+}
+
+}  // namespace gemm
+}  // namespace rl
 
 // ------------------------------------------------------------------------------------------------------------
 // SwiGLU MLP: the Qwen3-VL / DiT feed-forward as two packed-weight GEMMs through a caller workspace.

@@ -215,18 +215,21 @@ def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo
 
 
 def conv_k(cin, taps):
-    """The conv GEMM's K: taps^2 * Cin rounded up to a multiple of 64 (zero rows after the last tap)."""
-    return (taps * taps * cin + 63) // 64 * 64
+    """The conv GEMM's K: taps^2 taps of Cin channels, each rounded up to a multiple of 64 (zero rows)."""
+    return taps * taps * ((cin + 63) // 64 * 64)
 
 
 def conv_weight(w, bias=None, cout_pad=128):
     """Conv weight (Cout, Cin, k, k), k = 3 or 1, on the GPU -> (PackedWeight of B = [(dy, dx, ci)][co], bf16 bias or
-    None, taps). K is zero-padded to conv_k(Cin, k), Cout to a multiple of `cout_pad` (the GEMM's N tile)."""
+    None, taps). Each tap's Cin rows are zero-padded to a multiple of 64 (K = conv_k(Cin, k)), Cout to a multiple of
+    `cout_pad` (the GEMM's N tile)."""
     _check_cuda(w, bias)
     cout, cin, k, _ = w.shape
     n = (cout + cout_pad - 1) // cout_pad * cout_pad
-    B = torch.zeros((conv_k(cin, k), n), dtype=torch.float32, device=w.device)
-    B[:k * k * cin, :cout] = w.float().permute(2, 3, 1, 0).reshape(k * k * cin, cout)
+    kt = conv_k(cin, 1)
+    B = torch.zeros((k * k, kt, n), dtype=torch.float32, device=w.device)
+    B[:, :cin, :cout] = w.float().permute(2, 3, 1, 0).reshape(k * k, cin, cout)
+    B = B.reshape(k * k * kt, n)
     b = None
     if bias is not None:
         b = torch.zeros(n, dtype=torch.bfloat16, device=w.device)
