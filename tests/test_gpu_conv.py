@@ -1,6 +1,6 @@
 """GPU parity of the VAE decoder convolution (rl_conv2d_bfp16: the packed-weight GEMM on A tiles loaded from the
-image by 3-D TMA when W % 128 == 0, else on im2col-gathered rows) against the CPU oracle (oracle/vae_oracle.conv_ref = vae_ops.conv_ref on the bfp16-rounded activations and weights the reference's
-vconv multiplies). Output is bf16: max-rel <= 2e-3 + 2^-8 (the GEMM bar plus the output's own bf16 rounding)."""
+image by 3-D TMA when W % 128 == 0, else on im2col-gathered rows) against the CPU oracle (oracle/vae_oracle.conv_ref
+= vae_ops.conv_ref on the bfp16-rounded activations and weights the reference's vconv multiplies). Output is bf16: max-rel <= 2e-3 + 2^-8 (the GEMM bar plus the output's own bf16 rounding)."""
 
 import numpy as np
 import pytest
