@@ -2,7 +2,8 @@
 
     python -m redline_tiny_b200.profile_cases <case> [--iters N]
 
-cases: linear_c1 | quantize_c1 | swiglu_up_c2 | attention_c3 | qkv_post_c3 | ln_mod_c4 | dit_block_c4
+cases: linear_c1 | quantize_c1 | swiglu_up_c2 | attention_c3 | qkv_post_c3 | ln_mod_c4 | dit_block_c4 |
+       vae_conv_128x1152 | vae_conv_512x288 (3x3 convs of the VAE decoder: the implicit GEMM)
 Inputs are seeded synthetic tensors of the configs' shapes (a few hundred MB on the device at most).
 """
 
@@ -45,6 +46,15 @@ def main():
 
         def fn():
             ops.swiglu_up(x, w, out=h)
+    elif c in ("vae_conv_128x1152", "vae_conv_512x288"):
+        H, C = (128, 1152) if c == "vae_conv_128x1152" else (512, 288)
+        x = ops.quantize_bfp16(torch.randn((H * H, C), generator=g, device=dev), want_bytes=False)[1].view(H, H, C)
+        pw, bias, taps = ops.conv_weight(torch.randn((C, C, 3, 3), generator=g, device=dev) * 0.02,
+                                         torch.randn(C, generator=g, device=dev) * 0.01)
+        y = torch.empty((H, H, pw.N), dtype=torch.bfloat16, device=dev)
+
+        def fn():
+            ops.conv2d(x, pw, bias, taps, out=y)
     elif c in ("attention_c3", "qkv_post_c3", "ln_mod_c4", "dit_block_c4"):
         cfg = dit.DiTConfig(blocks=1)
         model = dit.DiT(cfg, dit.random_weights(cfg, seed=0))
