@@ -460,24 +460,30 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
 
-    extras = measure_configs(dev, stream, ws, seed=100 + rank) if not args.no_extras else {}
-    if ws > 1 and extras:   # max over ranks of every timing
-        flat = [v["ms"] for v in extras["C5_gemm_sweep_K3072_N12288"].values()] + [
-            extras[k]["ms"] for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step",
-                                      f"C4_dit_step_tp{ws}")]
+    extras = {}
+    if not args.no_extras:
+        # the other configs run right after the timed loop; their SM clock is sampled too (after the GEMM loop has
+        # reached the power cap the clock stays lowered for a while)
+        with ClockSampler(local) as clk_x:
+            extras = measure_configs(dev, stream, ws, seed=100 + rank)
+        extras["clocks"] = clk_x.summary()
+    if ws > 1 and extras:   # max over ranks of every timing (every rank holds the same keys)
+        keys = [k for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step", f"C4_dit_step_tp{ws}",
+                            f"C4_dit_step_tp{ws}_nccl_bf16") if k in extras]
+        sweep = extras["C5_gemm_sweep_K3072_N12288"]
+        flat = [v["ms"] for v in sweep.values()] + [extras[k]["ms"] for k in keys]
         tt = torch.tensor(flat, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         mx = tt.tolist()
-        for i, key in enumerate(extras["C5_gemm_sweep_K3072_N12288"]):
-            e = extras["C5_gemm_sweep_K3072_N12288"][key]
+        for i, key in enumerate(sweep):
+            e = sweep[key]
             e["TFLOP/s"] *= e["ms"] / mx[i]
             e["ms"] = mx[i]
-        for j, key in enumerate(("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step",
-                                 f"C4_dit_step_tp{ws}")):
+        for j, key in enumerate(keys):
             e = extras[key]
             rate = "TFLOP/s_all_gpus" if key.startswith("C4_dit_step_tp") else "TFLOP/s"
-            e[rate] *= e["ms"] / mx[4 + j]
-            e["ms"] = mx[4 + j]
+            e[rate] *= e["ms"] / mx[len(sweep) + j]
+            e["ms"] = mx[len(sweep) + j]
     if extras:
         extras["C4_dit_step"]["images_per_s_all_gpus"] = ws * 1e3 / extras["C4_dit_step"]["ms"]
         extras["note"] = ("per-GPU timings (max over ranks); each GPU runs its own copy (data-parallel); "
