@@ -467,6 +467,8 @@ def run_ours(args, ws, rank, local):
         with ClockSampler(local) as clk_x:
             extras = measure_configs(dev, stream, ws, seed=100 + rank)
         extras["clocks"] = clk_x.summary()
+        extras["device"] = {"sms": torch.cuda.get_device_properties(dev).multi_processor_count,
+                            "pair_gemm_clusters": L.lib().rl_gemm_pair_clusters()}
     if ws > 1 and extras:   # max over ranks of every timing (every rank holds the same keys)
         keys = [k for k in ("C2_swiglu_mlp", "C3_joint_attention_sublayer", "C4_dit_step", f"C4_dit_step_tp{ws}",
                             f"C4_dit_step_tp{ws}_nccl_bf16") if k in extras]

@@ -317,6 +317,9 @@ int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const u
  * (tcgen05.mma cta_group::2 over a cluster of two CTAs) with A in shared memory / TMEM; tuning codes
  * 1000*P + 100*G + 10*V + S (1313, 1125, 2125, 1224, 2224, 1333, 1234, 1346, 1448, 2248) also select the decode split
  * and the pipeline depth. Returns the previous value. */
+/* Resident 2-CTA clusters of the default pair GEMM kernel on the current device (two CTAs of a cluster share a GPC,
+ * so this follows the chip's GPC layout); 0 without an sm_100 device. The split-K choice uses it. */
+int rl_gemm_pair_clusters(void);
 int rl_set_gemm_variant(int variant);
 
 /* Attention kernel for tests and benchmarks: 0 = default (two 128-query tiles per CTA, the tensor pipe working on one

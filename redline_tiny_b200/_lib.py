@@ -34,6 +34,7 @@ SIGNATURES = {
     "rl_linear_bfp16_workspace": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),
     "rl_linear_bfp16_ws": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P, ctypes.c_size_t, _P]),
     "rl_set_gemm_variant": (_I, [_I]),
+    "rl_gemm_pair_clusters": (_I, []),
     "rl_set_attention_variant": (_I, [_I]),
     "rl_set_conv_path": (_I, [_I]),
     "rl_conv2d_workspace": (ctypes.c_size_t, [_I, _I, _I, _I]),

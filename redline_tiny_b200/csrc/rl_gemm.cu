@@ -762,6 +762,38 @@ int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
   return RL_OK;
 }
 
+// How many 2-CTA clusters of the pair kernel can be resident at once on the current device (cached per device). A
+// cluster's two CTAs share a GPC, so this depends on the chip's GPC layout, not only on the SM count.
+template <int V, int S, int G, int P>
+int pair_max_clusters(int* out) {
+  using C = pair::Cfg<V, S, G, P>;
+  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P>;
+  static int cached[64] = {0};
+  int dev = 0;
+  RL_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(RL_ERR_CUDA, "rl_linear_bfp16: device index %d", dev);
+  if (cached[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2);
+    RL_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    int n = 0;
+    RL_TRY_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+    if (n <= 0) return fail(RL_ERR_UNSUPPORTED, "rl_linear_bfp16: no CTA pair fits on this device");
+    cached[dev] = n;
+  }
+  *out = cached[dev];
+  return RL_OK;
+}
+
 // Pair kernel: clusters of two CTAs; the grid is as many clusters as can be resident at once (at most one per pair
 // tile), each walking pair tiles with stride = number of clusters.
 template <int V, int S, int G, int P>
@@ -782,20 +814,11 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(2 * 1);
-  static int max_clusters[64] = {0};
-  int dev = 0;
-  RL_TRY_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(RL_ERR_CUDA, "rl_linear_bfp16: device index %d", dev);
-  if (max_clusters[dev] == 0) {
-    RL_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    int n = 0;
-    RL_TRY_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
-    if (n <= 0) return fail(RL_ERR_UNSUPPORTED, "rl_linear_bfp16: no CTA pair fits on this device");
-    max_clusters[dev] = n;
-  }
+  int max_clusters = 0;
+  int st2 = pair_max_clusters<V, S, G, P>(&max_clusters);
+  if (st2 != RL_OK) return st2;
   const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2) * p.splits;
-  const int nclusters = ntiles < max_clusters[dev] ? ntiles : max_clusters[dev];
+  const int nclusters = ntiles < max_clusters ? ntiles : max_clusters;
   cfg.gridDim = dim3(2 * nclusters);
   RL_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p));
   RL_TRY_CUDA(cudaGetLastError());
@@ -837,10 +860,13 @@ int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) 
 }
 
 // Split-K for the pair kernel on a grid that would not fill the GPU: the largest S in {2, 4} with S x (pair tiles)
-// <= clusters (one pair of SMs each), KT % S == 0 and at least 16 K steps per split; 1 when no split helps.
+// <= the pair kernel's resident clusters (one pair of SMs each), KT % S == 0 and at least 16 K steps per split; 1
+// when no split helps (or no device answers the occupancy query).
 inline int choose_splits(int64_t M, int64_t K, int64_t N) {
   if (N % 256) return 1;
-  const int64_t clusters = sm_count() / 2;
+  int resident = 0;
+  if (pair_max_clusters<kTmemA, 8, 2, 2>(&resident) != RL_OK) return 1;
+  const int64_t clusters = resident;
   const int64_t tiles = (M + BN - 1) / BN * (N / 256);
   const int64_t KT = K / BK;
   int S = 1;
@@ -929,6 +955,11 @@ int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w
       out_dtype == RL_F32 ? 1 : 0);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
+}
+
+int rl_gemm_pair_clusters(void) {
+  int n = 0;
+  return rl::gemm::pair_max_clusters<rl::gemm::kTmemA, 8, 2, 2>(&n) == RL_OK ? n : 0;
 }
 
 int rl_set_gemm_variant(int variant) {
