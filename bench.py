@@ -342,8 +342,9 @@ def measure_configs(dev, stream, ws, seed):
         lat1 = torch.randn((cfg.image, cfg.latent_ch), generator=torch.Generator(device=dev).manual_seed(7),
                            device=dev)
         txt1 = torch.randn((cfg.text, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(8), device=dev)
-        # the default reduction (at 2 GPUs: the LayerNorm kernel sums the peers' bf16 partials over NVLink; else an
-        # NCCL all-reduce of the bf16 partials), and at 2 GPUs the NCCL all-reduce beside it
+        # the default reduction (at 2 GPUs: the projection GEMM stores its bf16 partial into the other rank's memory
+        # and the LayerNorm kernel adds both; else an NCCL all-reduce of the bf16 partials), and at 2 GPUs the NCCL
+        # all-reduce beside it
         for mode in (["auto", "bf16"] if ws == 2 else ["auto"]):
             w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
             tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD),
@@ -355,7 +356,7 @@ def measure_configs(dev, stream, ws, seed):
             key = f"C4_dit_step_tp{ws}" + ("" if mode == "auto" else "_nccl_bf16")
             out[key] = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
                         "reductions_per_step": 2 * cfg.blocks, "partial_bytes": cfg.M * cfg.hidden * 2,
-                        "reduction": "peer reads in the LayerNorm kernel" if tp_model.reduce_dtype == "peer"
+                        "reduction": "fused: GEMM peer stores + LayerNorm sum" if tp_model.reduce_dtype == "peer"
                         else "NCCL all-reduce, bf16"}
             tp_model.close()
             del tp_model
