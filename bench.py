@@ -16,7 +16,6 @@ restated in oracle/bfp16_oracle.py) on the host cores, on a bounded row sample p
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time

@@ -18,7 +18,6 @@ attend to the valid keys only and their outputs are not used.
 
 import math
 
-import numpy as np
 import torch
 
 from . import ops

@@ -5,8 +5,6 @@ The kernel's output is rounded to bfp16 blocks of 8 along the head dim (the out-
 compared with the oracle rounded the same way: max-rel <= 2e-2 (one bfp16 step is 2^-7 of a block maximum, and P is
 bf16) and correlation > 0.9999 (the reference asks corr > 0.995, run_attn.py:218)."""
 
-import math
-
 import numpy as np
 import pytest
 
