@@ -112,6 +112,19 @@ int rl_pack_weights(const void* B, int dtype, int64_t K, int64_t N, int swiglu_i
                     rl_stream_t stream);
 
 /*
+ * Column shard `rank` of `world` of a packed B (K, N) for the N-split standalone GEMM: columns
+ * [n0, n0 + n_cols) = [rank * N / world, (rank + 1) * N / world) are the contiguous bytes
+ * [byte_offset, byte_offset + byte_count) of both the reference's pack_b stream and the native format, because both
+ * store 128-column strips whole, N-tile outer (b_layout, redline/npu_layouts.py:11-16; pack_b,
+ * redline/pack_weights.py:72-79). So a rank streams its shard in place, without repacking, and its GEMM output is
+ * C[:, n0 : n0 + n_cols]. Needs K % 64 == 0 and N % (128 * world) == 0 (the 2-SM pair GEMM kernel also wants
+ * n_cols % 256 == 0; other shards run the 1-SM kernel). Host arithmetic only: no device is touched. Up matrices
+ * packed with swiglu_interleaved keep each [gate 64 | proj 64] tile whole, so a shard holds n_cols / 2 FFN units.
+ */
+int rl_weights_shard(int64_t K, int64_t N, int rank, int world, int64_t* n0, int64_t* n_cols, int64_t* byte_offset,
+                     int64_t* byte_count);
+
+/*
  * a7/a8/a9 - the packed-weight GEMM. Replaces gemm(npu, w, op, M, a, c) (redline/forward.py:194-197), which runs
  * matmul_vectorized_bfp16 (kernels/atb3/mm_bfp_rho.cc:64-177) and, for the up projection,
  * matmul_swiglu_bfp16 (kernels/atb3/mm_bfp_swiglu.cc:88-168).
@@ -231,6 +244,13 @@ int rl_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64
 int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
                      int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
                      int64_t ldo, rl_stream_t stream);
+
+/* rl_attention_gqa with o (Nq, ldo) fp32 = O / l before its bfp16 rounding (ldo % 8 == 0, 16-byte aligned): the
+ * attention kernel's own result, for callers that keep the output in fp32 and for checks of the kernel against the
+ * float64 softmax without the output rounding in between (run_attn.py:203-209 compares the same quantity). */
+int rl_attention_gqa_f32(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
+                         int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, float* o,
+                         int64_t ldo, rl_stream_t stream);
 
 /*
  * VAE decoder convolution, 3x3 pad 1 (taps = 3) or 1x1 (taps = 1), stride 1, with bfp16 weights. Replaces the vconv

@@ -4,8 +4,9 @@ legs, never by the product package).
 Composes the restated reference ops of bfp16_oracle.py in the order of the reference's block loop
 (redline/forward.py:240-254) and step (forward.py:396-412, 256-269, 58-61), rounding where the stored tensors are
 rounded: GEMM outputs and QK-norm/RoPE outputs to bf16, LayerNorm outputs, the attention output and the SwiGLU output
-to bfp16 (blocks of 8 along the row), exactly as the GPU pipeline stores them. The adaLN modulation comes from the
-host glue (redline_tiny_b200.host_glue, pinned against the reference by tests/golden).
+to bfp16 (blocks of 8 along the row), exactly as the GPU pipeline stores them. The adaLN modulation comes from
+oracle/host_oracle.py, the RoPE table and token layout from the host glue the product uses
+(redline_tiny_b200.host_glue); both are pinned against the reference by tests/golden.
 """
 
 import math
@@ -13,6 +14,7 @@ import math
 import numpy as np
 
 from . import bfp16_oracle as O
+from . import host_oracle as HO
 
 HEAD_DIM = 128
 C_LOG2 = math.log2(math.e) / math.sqrt(HEAD_DIM)
@@ -61,9 +63,9 @@ def forward(cfg, prep, latents, text_states, sigma, host_glue, reduce=None):
     projection output over the ranks (an all-reduce) before it is rounded to bf16."""
     D, M, T = cfg.hidden, cfg.M, cfg.text
     reduce = reduce or (lambda c: c)
-    te = host_glue.temb(prep["host"], host_glue.model_t(sigma))
-    mod = host_glue.modulation(prep["host"], te)
-    out_scale = host_glue.norm_out_scale(prep["host"], te)
+    te = HO.temb(prep["host"], host_glue.model_t(sigma))
+    mod = HO.modulation(prep["host"], te)
+    out_scale = HO.norm_out_scale(prep["host"], te)
     s1, g1, s2, g2 = (mod[:, i * D:(i + 1) * D] for i in range(4))
 
     def lp(g, sc):

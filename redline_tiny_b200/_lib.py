@@ -30,6 +30,8 @@ SIGNATURES = {
     "rl_permute_bf16": (_I, [_P, _I, _P, _I, _I64, _I64, _P]),
     "rl_weights_from_pack_b": (_I, [_P, _I64, _I64, _I, _P, _P]),
     "rl_pack_weights": (_I, [_P, _I, _I64, _I64, _I, _P, _P]),
+    "rl_weights_shard": (_I, [_I64, _I64, _I, _I, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                              ctypes.POINTER(_I64)]),
     "rl_linear_bfp16": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P]),
     "rl_linear_bfp16_workspace": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),
     "rl_linear_bfp16_ws": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _I, _P, ctypes.c_size_t, _P]),
@@ -48,6 +50,7 @@ SIGNATURES = {
     "rl_qkv_post_gqa": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _I64, _P]),
     "rl_rms_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "rl_attention_gqa": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),
+    "rl_attention_gqa_f32": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),
     "rl_swiglu_mlp": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P]),
     "rl_matvec_f32": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "rl_sinusoidal_embed": (_I, [ctypes.c_float, ctypes.c_float, _P, _I, _P, _P]),

@@ -68,6 +68,7 @@ struct Params {
   const int32_t* row_limit;   // per query row: last visible key (inclusive), or null
   float scale_log2;           // logits = (q . k) * scale_log2, in log2 units (> 0)
   uint16_t* o;
+  float* o32;                 // when set: O / l written unrounded in fp32 here instead of bfp16-rounded bf16 to o
   int64_t ldo;
   int nblk;
 };
@@ -347,11 +348,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       uint16_t* orow = p.o + qrow * p.ldo + static_cast<int64_t>(h) * HD;
+      float* orow32 = p.o32 ? p.o32 + qrow * p.ldo + static_cast<int64_t>(h) * HD : nullptr;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         RL_TMEM_LD32(t_o + lane_off + 32 * c, o);
         tmem_ld_wait_regs(o);
+        if (orow32) {
+          if (qrow < p.Nq) {
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+              reinterpret_cast<float4*>(orow32 + 32 * c + 4 * b)[0] =
+                  make_float4(__uint_as_float(o[4 * b]) * inv, __uint_as_float(o[4 * b + 1]) * inv,
+                              __uint_as_float(o[4 * b + 2]) * inv, __uint_as_float(o[4 * b + 3]) * inv);
+          }
+          continue;
+        }
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
           uint32_t bits[8];
@@ -461,13 +473,23 @@ __device__ __forceinline__ void softmax_block(uint32_t ta, uint32_t to, int64_t 
 }
 
 // O / l of the thread's query row, rounded to bfp16 blocks of 8 along the head dim, stored row-major.
-__device__ __forceinline__ void store_o_row(uint32_t to, float l_run, uint16_t* orow, bool store) {
+__device__ __forceinline__ void store_o_row(uint32_t to, float l_run, uint16_t* orow, float* orow32, bool store) {
   const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t o[32];
     RL_TMEM_LD32(to + 32 * c, o);
     tmem_ld_wait_regs(o);
+    if (orow32) {
+      if (store) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b)
+          reinterpret_cast<float4*>(orow32 + 32 * c + 4 * b)[0] =
+              make_float4(__uint_as_float(o[4 * b]) * inv, __uint_as_float(o[4 * b + 1]) * inv,
+                          __uint_as_float(o[4 * b + 2]) * inv, __uint_as_float(o[4 * b + 3]) * inv);
+      }
+      continue;
+    }
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       uint32_t bits[8];
@@ -707,7 +729,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && nblk > 0 && mbar_wait(&bars->o_full, 0, abort)) {
       tc_fence_after();
-      store_o_row(to, l_run, p.o + qrow * p.ldo + static_cast<int64_t>(h) * HD, qrow < p.Nq);
+      const int64_t ooff = qrow * p.ldo + static_cast<int64_t>(h) * HD;
+      store_o_row(to, l_run, p.o + ooff, p.o32 ? p.o32 + ooff : nullptr, qrow < p.Nq);
     }
   }
 
@@ -776,20 +799,21 @@ inline int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 }  // namespace attn
 }  // namespace rl
 
-extern "C" {
+namespace rl {
+namespace attn {
 
-int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
-                     int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
-                     int64_t ldo, rl_stream_t stream) {
-  using namespace rl;
-  using namespace rl::attn;
-  RL_REQUIRE(q && k && vt && o, RL_ERR_ARGUMENT, "rl_attention: NULL pointer");
+// The attention entry points: O / l rounded to bfp16 blocks of 8 as bf16 into o, or unrounded fp32 into o32.
+int run(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv, int64_t Nq, int64_t Nk,
+        int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o, float* o32, int64_t ldo,
+        cudaStream_t stream) {
+  RL_REQUIRE(q && k && vt && (o || o32), RL_ERR_ARGUMENT, "rl_attention: NULL pointer");
   RL_REQUIRE(H > 0 && Nq >= 0 && Nk > 0 && nkv >= 0 && nkv <= Nk && ldv >= Nk && ldv % 8 == 0, RL_ERR_ARGUMENT,
              "rl_attention: need 0 <= nkv <= Nk <= ldv, ldv %% 8 == 0");
   RL_REQUIRE(Hkv > 0 && H % Hkv == 0, RL_ERR_ARGUMENT, "rl_attention: %d query heads over %d K/V heads", H, Hkv);
   RL_REQUIRE(ldo >= static_cast<int64_t>(H) * HD && ldo % 8 == 0, RL_ERR_ARGUMENT,
              "rl_attention: ldo must be >= H * 128 and a multiple of 8");
-  RL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(vt, 16) && aligned(o, 16) && aligned(row_limit, 4),
+  RL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(vt, 16) && aligned(o, 16) && aligned(o32, 16) &&
+                 aligned(row_limit, 4),
              RL_ERR_ALIGNMENT, "rl_attention: q, k, vt, o must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_attention: needs an sm_100 device");
   if (Nq == 0) return RL_OK;
@@ -807,10 +831,13 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
   p.row_limit = row_limit;
   p.scale_log2 = scale_log2;
   p.o = o;
+  p.o32 = o32;
   p.ldo = ldo;
   p.nblk = static_cast<int>((nkv + BKV - 1) / BKV);
   if (p.nblk == 0) {  // no visible key: the output is zero
-    RL_TRY_CUDA(cudaMemset2DAsync(o, ldo * 2, 0, static_cast<size_t>(H) * HD * 2, Nq, stream));
+    const size_t es = o32 ? 4 : 2;
+    RL_TRY_CUDA(cudaMemset2DAsync(o32 ? static_cast<void*>(o32) : static_cast<void*>(o), ldo * es, 0,
+                                  static_cast<size_t>(H) * HD * es, Nq, stream));
     return RL_OK;
   }
   int v = variant();
@@ -839,6 +866,25 @@ int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, i
   }
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
+}
+
+}  // namespace attn
+}  // namespace rl
+
+extern "C" {
+
+int rl_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
+                     int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, uint16_t* o,
+                     int64_t ldo, rl_stream_t stream) {
+  RL_REQUIRE(o, RL_ERR_ARGUMENT, "rl_attention: NULL pointer");
+  return rl::attn::run(q, k, vt, ldv, H, Hkv, Nq, Nk, nkv, row_limit, scale_log2, o, nullptr, ldo, stream);
+}
+
+int rl_attention_gqa_f32(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int64_t ldv, int H, int Hkv,
+                         int64_t Nq, int64_t Nk, int64_t nkv, const int32_t* row_limit, float scale_log2, float* o,
+                         int64_t ldo, rl_stream_t stream) {
+  RL_REQUIRE(o, RL_ERR_ARGUMENT, "rl_attention_gqa_f32: NULL pointer");
+  return rl::attn::run(q, k, vt, ldv, H, Hkv, Nq, Nk, nkv, row_limit, scale_log2, nullptr, o, ldo, stream);
 }
 
 int rl_set_attention_variant(int variant) {

@@ -453,4 +453,20 @@ int rl_pack_weights(const void* B, int dtype, int64_t K, int64_t N, int swiglu_i
   return RL_OK;
 }
 
+int rl_weights_shard(int64_t K, int64_t N, int rank, int world, int64_t* n0, int64_t* n_cols, int64_t* byte_offset,
+                     int64_t* byte_count) {
+  RL_REQUIRE(n0 && n_cols && byte_offset && byte_count, RL_ERR_ARGUMENT, "rl_weights_shard: NULL pointer");
+  RL_REQUIRE(world > 0 && rank >= 0 && rank < world, RL_ERR_ARGUMENT, "rl_weights_shard: rank %d of %d", rank, world);
+  RL_REQUIRE(K > 0 && K % 64 == 0 && N > 0 && N % (128 * static_cast<int64_t>(world)) == 0, RL_ERR_ARGUMENT,
+             "rl_weights_shard: need K %% 64 == 0 and N %% (128 * world) == 0 (K=%lld N=%lld world=%d)", (long long)K,
+             (long long)N, world);
+  // one 128-column strip = K / 64 tiles of 9216 bytes, contiguous in both the b_layout stream and the native format
+  const int64_t cols = N / world, strip = K / 64 * 9216;
+  *n0 = rank * cols;
+  *n_cols = cols;
+  *byte_offset = (rank * cols / 128) * strip;
+  *byte_count = cols / 128 * strip;
+  return RL_OK;
+}
+
 }  // extern "C"

@@ -1,8 +1,9 @@
-"""Per-step host glue of the DiT, on the CPU in numpy float32 (tiny matvecs and tables).
-
-These run on the host in the reference as well (redline/host_glue.py; forward.py:47-61; run_qkv.py:37-50). They
-produce the inputs of the GPU epilogues: the adaLN gate / scale rows, the 3-axis RoPE cos/sin table and the row
-positions. Each function cites the reference line it restates; tests pin them against the reference's outputs.
+"""Host-side tables and schedule of the DiT, in numpy (computed once per model or per step, as in the reference:
+redline/host_glue.py; forward.py:47-61; run_qkv.py:37-50): the sigma schedule and the transformer's timestep, the
+Euler update, the sinusoidal frequencies the GPU conditioning kernels read, the joint token layout, the 3-axis RoPE
+cos/sin table and the row positions. The per-step conditioning products themselves run on the GPU
+(csrc/rl_adaln.cu). Each function cites the reference line it restates; tests pin them against the reference's
+outputs.
 """
 
 import math
@@ -31,61 +32,22 @@ def euler(latents, v, i, sigmas=SIGMAS):
     return latents + (nxt - sigmas[i]) * v
 
 
-def silu(x):
-    return x / (1 + np.exp(-x))
-
-
-def _linear(x, w, b=None):
-    y = x @ w.T
-    return y + b if b is not None else y
-
-
 def timestep_freqs(half=128):
     """The sinusoidal embedding's frequencies exp(-ln(10^4) i / half), float32 (host_glue.py:31-36)."""
     return np.exp(-math.log(10000) * np.arange(half, dtype=np.float32) / half)
 
 
-def temb(w, t):
-    """Sinusoidal(256) -> linear_1 -> SiLU -> linear_2 on rows [t, 0] (host_glue.py:31-40)."""
-    ts = np.array([t, 0.0], np.float32) * 1000.0
-    freqs = timestep_freqs()
-    arg = ts[:, None] * freqs[None]
-    e = np.concatenate([np.cos(arg), np.sin(arg)], -1).astype(np.float32)
-    p = "time_text_embed.timestep_embedder."
-    h = silu(_linear(e, w[p + "linear_1.weight"], w.get(p + "linear_1.bias")))
-    return _linear(h, w[p + "linear_2.weight"], w.get(p + "linear_2.bias"))
-
-
-def modulation(w, te):
-    """Linear(SiLU(temb)) -> (2, 4 * HID) = [scale1 | gate1 | scale2 | gate2] (host_glue.py:43-44)."""
-    return _linear(silu(te), w["modulation.1.weight"])
-
-
-def norm_out_scale(w, te):
-    """host_glue.py:47-48."""
-    return _linear(silu(te), w["norm_out.linear.weight"])
-
-
-def adaln_params(mod, out_scale, D):
-    """The LayerNorm parameter sets of one step (forward.py:231-238), float32 (2, 2, D) = rows [g | sc] before their
-    bf16 rounding: first (1, 1 + scale1), mlp (tanh gate1, 1 + scale2), attn (tanh gate2, 1 + scale1),
-    out (tanh gate2, 1 + out_scale); mod = [scale1 | gate1 | scale2 | gate2]."""
-    s1, g1, s2, g2 = (np.asarray(mod[:, i * D:(i + 1) * D], np.float32) for i in range(4))
-    out_scale = np.asarray(out_scale[:, :D], np.float32)
-
-    def lp(g, sc):
-        return np.concatenate([np.asarray(g, np.float32), np.asarray(sc, np.float32)], 1).reshape(2, 2, D)
-    return {"first": lp(np.ones((2, D)), 1 + s1), "mlp": lp(np.tanh(g1), 1 + s2),
-            "attn": lp(np.tanh(g2), 1 + s1), "out": lp(np.tanh(g2), 1 + out_scale)}
-
-
 def joint_layout(vlm_image_mask, n_target=4096, grid=(64, 64)):
-    """The joint sequence: text positions, image slots expanded to 2x2 latent tokens, then the target's tokens
-    (host_glue.py:59-65). Returns (image_pad_mask, img_shapes). `grid` is the latent token grid of each image
-    (64 x 64 at 1024^2, the only size the reference supports; smaller grids serve reduced test configurations)."""
-    m = np.concatenate([np.asarray(vlm_image_mask, bool).ravel(), np.ones(n_target // 4, bool)])
-    pad = np.repeat(m, np.where(m, 4, 1))
-    return pad, [(1, grid[0], grid[1])] * (int(pad.sum()) // n_target)
+    """The joint sequence of the reference's host_glue.joint_layout (host_glue.py:59-65): every text position of the
+    VLM sequence is one token, every image slot of it stands for a 2 x 2 patch of latent tokens, and the target
+    image's n_target tokens follow. Returns (image_pad_mask, img_shapes): the per-token image flag and one
+    (1, h, w) latent grid per image, the target's included. `grid` is that grid (64 x 64 at 1024^2, the only size
+    the reference supports; smaller grids serve reduced test configurations)."""
+    slots = np.asarray(vlm_image_mask, bool).ravel()
+    tokens_per_slot = 1 + 3 * slots.astype(np.int64)              # 1 for text, 4 for an image slot
+    is_img = np.concatenate([np.repeat(slots, tokens_per_slot), np.ones(n_target, bool)])
+    images = int(is_img.sum()) // n_target
+    return is_img, [(1, grid[0], grid[1])] * images
 
 
 def rope(image_pad_mask, img_shapes, axes=(16, 56, 56), theta=10000):

@@ -112,6 +112,21 @@ class PackedWeight:
         L.call("rl_pack_weights", _ptr(B), _dtype_code(B), K, N, int(swiglu), _ptr(native), _stream())
         return cls(native, K, N, swiglu)
 
+    def shard(self, rank, world):
+        """Columns [n0, n0 + N / world) of this weight as a view of its own bytes (no copy): the N-split standalone
+        GEMM's operand on GPU `rank`. Returns (PackedWeight, n0)."""
+        n0, cols, off, count = weights_shard(self.K, self.N, rank, world)
+        return PackedWeight(self.native.narrow(0, off, count), self.K, cols, self.swiglu), n0
+
+
+def weights_shard(K, N, rank, world):
+    """(n0, n_cols, byte_offset, byte_count) of column shard `rank` of `world` of a packed B (K, N): the same bytes
+    in the reference's pack_b stream and in the native tiles (rl_weights_shard)."""
+    import ctypes
+    v = [ctypes.c_int64() for _ in range(4)]
+    L.call("rl_weights_shard", int(K), int(N), int(rank), int(world), *[ctypes.byref(x) for x in v])
+    return tuple(x.value for x in v)
+
 
 def linear_bfp16(x_dq, w, bias=None, out=None, out_dtype=torch.bfloat16):
     """C = x_dq @ B (+ bias), x_dq = bf16 (M, K) holding bfp16 values (quantize_bfp16's decoded output)."""
@@ -193,10 +208,11 @@ def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
     return q, k, vt
 
 
-def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo=None):
-    """Flash attention per head: q (H, Nq, 128), k (Hkv, Nk, 128), vt (Hkv, 128, ldv) bf16 -> o (Nq, ldo) bf16 with
-    head h at columns 128h.. (rounded to bfp16 along the head dim); with Hkv < H query head h reads K/V head
-    h / (H / Hkv) (grouped-query attention). scale_log2 defaults to log2(e)/sqrt(128)."""
+def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo=None, out_dtype=torch.bfloat16):
+    """Flash attention per head: q (H, Nq, 128), k (Hkv, Nk, 128), vt (Hkv, 128, ldv) bf16 -> o (Nq, ldo) with
+    head h at columns 128h..; bf16 rounded to bfp16 along the head dim (the out-projection's A operand), or with
+    out_dtype=torch.float32 the unrounded fp32 O / l. With Hkv < H query head h reads K/V head h / (H / Hkv)
+    (grouped-query attention). scale_log2 defaults to log2(e)/sqrt(128)."""
     import math
     _check_cuda(q, k, vt, row_limit, out)
     H, Nq, _ = q.shape
@@ -206,11 +222,12 @@ def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo
     scale_log2 = math.log2(math.e) / math.sqrt(128) if scale_log2 is None else float(scale_log2)
     ldo = ldo or H * 128
     if out is None:
-        out = torch.empty((Nq, ldo), dtype=torch.bfloat16, device=q.device)
+        out = torch.empty((Nq, ldo), dtype=out_dtype, device=q.device)
     if row_limit is not None and row_limit.dtype != torch.int32:
         raise ValueError("row_limit must be int32")
-    L.call("rl_attention_gqa", _ptr(q), _ptr(k), _ptr(vt), ldv, H, k.shape[0], Nq, Nk, nkv, _ptr(row_limit),
-           scale_log2, _ptr(out), ldo, _stream())
+    fn = "rl_attention_gqa_f32" if out.dtype == torch.float32 else "rl_attention_gqa"
+    L.call(fn, _ptr(q), _ptr(k), _ptr(vt), ldv, H, k.shape[0], Nq, Nk, nkv, _ptr(row_limit), scale_log2, _ptr(out),
+           ldo, _stream())
     return out
 
 

@@ -230,6 +230,18 @@ def main(ref_root):
     limn = rn.integers(0, 250, 64).astype(np.int32)
     out["npu_lim"], out["npu_limpack"] = limn, ra.pack_lim(limn, 64, 64)
 
+    # --- attention: the reference's float64 causal GQA attention (vlm_run.attn_ref, vlm_run.py:181-190; 32 query
+    # heads over 8 K/V heads) on bf16 inputs, own generator; inputs stored as bf16 bit patterns
+    import vlm_run as vr
+    ra_ = np.random.default_rng(31)
+    na = 40
+    qa = ra_.standard_normal((vr.HQ, na, vr.HD)).astype(bfloat16)
+    ka = ra_.standard_normal((vr.HKV, na, vr.HD)).astype(bfloat16)
+    va = ra_.standard_normal((vr.HKV, na, vr.HD)).astype(bfloat16)
+    out["attn_q_bf16"], out["attn_k_bf16"], out["attn_v_bf16"] = (a.view(np.uint16) for a in (qa, ka, va))
+    out["attn_ref"] = vr.attn_ref(qa.astype(np.float32), ka.astype(np.float32), va.astype(np.float32),
+                                  na).astype(np.float32)
+
     dst = Path(__file__).with_name("golden.npz")
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size / 1e3:.0f} KB, {len(out)} arrays)")

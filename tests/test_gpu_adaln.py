@@ -5,6 +5,7 @@ norm_out, LayerNorm parameter rows)."""
 import numpy as np
 import pytest
 
+from oracle import host_oracle as HO
 from redline_tiny_b200 import host_glue as HG
 
 pytestmark = pytest.mark.gpu
@@ -67,7 +68,7 @@ def test_adaln_params_match_host_rows(env, golden):
            params["mlp"].data_ptr(), params["attn"].data_ptr(), params["out"].data_ptr(),
            torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    ref = HG.adaln_params(golden["mod_05"], golden["normout_05"], D)
+    ref = HO.adaln_params(golden["mod_05"], golden["normout_05"], D)
     for k, p in params.items():
         got = p.view(torch.int16).cpu().numpy().astype(np.int32) & 0xFFFF
         want = torch.from_numpy(ref[k]).to(torch.bfloat16).view(torch.int16).numpy().astype(np.int32) & 0xFFFF

@@ -58,6 +58,69 @@ def test_dit_config4_architecture_one_block():
     _check(cfg, sigma_index=3, seed=1)
 
 
+def _decoded_on_gpu(B):
+    """Float B (K, N) on the GPU -> its bfp16-decoded values (blocks of 8 consecutive K per column) as float32 numpy,
+    the operand oracle/dit_oracle.decode_b computes on the CPU: here the device quantiser (bit-exact against the
+    reference's to_bfp16, tests/test_gpu_codec.py) decodes the 4.8 G weights of 32 blocks, which numpy would take
+    minutes for."""
+    import torch
+    from redline_tiny_b200 import ops
+    _, dq = ops.quantize_bfp16(B.t().contiguous(), want_bytes=False)
+    return dq.t().float().cpu().numpy()
+
+
+class _LazyBlocks:
+    """The oracle's per-block operands, decoded one block at a time (the 32 blocks' float32 operands would need
+    19 GB of host memory)."""
+
+    def __init__(self, blocks):
+        self.blocks = blocks
+
+    def __len__(self):
+        return len(self.blocks)
+
+    def __iter__(self):
+        from redline_tiny_b200 import dit
+        for b in self.blocks:
+            yield {"qkv": _decoded_on_gpu(b["qkv"]), "o": _decoded_on_gpu(b["o"]),
+                   "up": _decoded_on_gpu(dit.interleave_up_torch(b["gate"], b["proj"])),
+                   "down": _decoded_on_gpu(b["down"]),
+                   "wq": (b["norm_q"].cpu().numpy().astype(np.float32) * np.float32(DO.C_LOG2)).astype(np.float32),
+                   "wk": b["norm_k"].cpu().numpy().astype(np.float32)}
+
+
+def test_dit_32_blocks_latent_matches_oracle():
+    """The whole 32-block transformer of config 4 (hidden 3072, 24 x 128 heads, SwiGLU FFN 12288, adaLN at the step's
+    sigma) on a reduced token count - 64 text + 256 image tokens on a 16 x 16 grid - so that the CPU oracle
+    (oracle/dit_oracle.forward: the reference's block loop forward.py:240-254 x 32, norm_out + proj_out 261-269, Euler
+    58-61) finishes in about a minute. This is where bf16 / bfp16 rounding differences could grow from block to
+    block, which the one-block tests cannot show: the latent after the Euler step and the velocity itself must both
+    reach cosine >= 0.999 against the oracle."""
+    import torch
+    from redline_tiny_b200 import dit, host_glue as HG, ops
+    cfg = dit.DiTConfig(text=64, image=256, grid=(16, 16))
+    assert cfg.blocks == 32 and cfg.hidden == 3072 and cfg.ffn == 12288
+    w = dit.random_weights(cfg, seed=4)
+    model = dit.DiT(cfg, w)
+    rng = np.random.default_rng(4)
+    lat = rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32)
+    txt = rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32)
+    i = 5                                     # sigma 0.845148 -> 0.704534: dt = -0.14
+    sig, nxt = HG.SIGMAS[i], HG.SIGMAS[i + 1]
+    v = model.forward(torch.from_numpy(lat), torch.from_numpy(txt), sig).float().cpu().numpy()
+    lat1 = model.denoise_step(torch.from_numpy(lat), torch.from_numpy(txt), i).cpu().numpy()
+    ops.device_status()
+    del model
+    torch.cuda.empty_cache()
+    prep = {"blocks": _LazyBlocks(w["blocks"]), "img_in": _decoded_on_gpu(w["img_in"]),
+            "proj_out": _decoded_on_gpu(w["proj_out"]), "host": w["host"]}
+    ref = DO.forward(cfg, prep, lat, txt, sig, HG)
+    ref_lat = HG.euler(lat, ref, i)
+    cv, cl = _cos(v, ref), _cos(lat1, ref_lat)
+    assert np.allclose(lat1, lat + (nxt - sig) * v, rtol=1e-5, atol=1e-5)
+    assert cv >= 0.999 and cl >= 0.999, f"32 blocks: velocity cos {cv:.6f}, latent cos {cl:.6f}"
+
+
 def test_dit_full_step_runs():
     """All 32 blocks of config 4 on the GPU: finite velocity of the expected shape (size-independent check; the
     block math is pinned by the two tests above)."""

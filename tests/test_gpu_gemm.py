@@ -192,3 +192,41 @@ def test_linear_mirror_stores_identical_copy(env, N):
     with pytest.raises(L.RedlineError):
         L.call("rl_linear_bfp16_mirror", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE,
                out.data_ptr(), mir.data_ptr(), L.RL_F32, s)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_n_sharded_gemm_equals_unsharded_columns(env, world):
+    """The N-split standalone GEMM (each GPU streams the contiguous bytes of its N / world weight columns and computes
+    C[:, its columns], no collective): every shard's output equals the unsharded GEMM's columns bit for bit, at
+    config 1's full size (X[4352, 3072] @ W[3072, 12288] + bias, bf16 out), both from the native tiles and from the
+    reference's own pack_b bytes cut at rl_weights_shard's offsets. The shards run one after another on one GPU: the
+    split needs no peer, so this is the multi-GPU path's arithmetic; the oracle checks sampled rows of each shard."""
+    torch, ops, dev = env
+    x, W, b = _case(4352, 3072, 12288, seed=21)
+    M, K = x.shape
+    N = W.shape[1]
+    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+    packed = torch.from_numpy(O.pack_b(W)).to(dev)
+    w = ops.PackedWeight.from_pack_b(packed, K, N)
+    bt = torch.from_numpy(b).to(dev).to(torch.bfloat16)
+    full = ops.linear_bfp16(dq, w, bias=bt)
+    rows = np.r_[0:8, 2040:2056, 4344:4352]
+    _, xd = O.quantize_rows(x[rows])
+    wd = O.unpack_b(O.pack_b(W), K, N)
+    covered = 0
+    for r in range(world):
+        ws, n0 = w.shard(r, world)
+        n1 = n0 + ws.N
+        assert n0 == covered and ws.N == N // world
+        covered = n1
+        c = ops.linear_bfp16(dq, ws, bias=bt[n0:n1].contiguous())
+        _, _, off, count = ops.weights_shard(K, N, r, world)
+        wr = ops.PackedWeight.from_pack_b(packed[off:off + count].contiguous(), K, N // world)
+        c2 = ops.linear_bfp16(dq, wr, bias=bt[n0:n1].contiguous())
+        ops.device_status()
+        assert torch.equal(c, full[:, n0:n1]), f"shard {r}/{world} differs from the unsharded columns"
+        assert torch.equal(c2, c), f"shard {r}/{world} from the reference's pack_b bytes differs"
+        ref = O.linear(xd, wd[:, n0:n1], b[n0:n1])
+        err = O.max_rel(c.float().cpu().numpy()[rows], ref)
+        assert err <= BF16_OUT_TOL, f"shard {r}/{world}: max-rel {err:.3e}"
+    assert covered == N

@@ -7,6 +7,7 @@ import numpy as np
 import pytest
 
 from oracle import bfp16_oracle as O
+from oracle import host_oracle as HO
 from redline_tiny_b200 import host_glue as HG
 
 
@@ -125,10 +126,10 @@ def test_host_glue_rope_tables(golden):
 
 def test_host_glue_temb_modulation(golden):
     w = {k[4:]: v for k, v in golden.items() if k.startswith("hw::")}
-    te = HG.temb(w, HG.model_t(0.5))
+    te = HO.temb(w, HG.model_t(0.5))
     assert np.array_equal(te, golden["temb_05"])
-    assert np.array_equal(HG.modulation(w, te), golden["mod_05"])
-    assert np.array_equal(HG.norm_out_scale(w, te), golden["normout_05"])
+    assert np.array_equal(HO.modulation(w, te), golden["mod_05"])
+    assert np.array_equal(HO.norm_out_scale(w, te), golden["normout_05"])
     assert np.array_equal(np.array([HG.model_t(s) for s in HG.SIGMAS]), golden["model_t"])
 
 
@@ -162,3 +163,21 @@ def test_npu_attention_formats(golden):
     for got, name in ((cos, "npu_cos"), (sin, "npu_sin"), (wq, "npu_wq"), (wk, "npu_wk")):
         assert np.array_equal(got, golden[name]), name
     assert np.array_equal(N.lim_pack(golden["npu_lim"]), golden["npu_limpack"])
+
+
+def attn_golden_inputs(g):
+    """The golden attention case as float32 arrays: q (32, n, 128), k / v (8, n, 128), all bf16 values."""
+    return tuple(O.bf16_from_bits(g[k]).astype(np.float32) for k in ("attn_q_bf16", "attn_k_bf16", "attn_v_bf16"))
+
+
+def test_attention_oracle_matches_reference_attn_ref(golden):
+    """oracle.attention_f64 (the float64 softmax used by every attention parity test) against the reference's own
+    float64 causal GQA attention, vlm_run.attn_ref (redline/vlm_run.py:181-190): query head h reads K/V head h // 4
+    and row r sees keys <= r (the per-row key limit form, run_attn.py:123-126)."""
+    q, k, v = attn_golden_inputs(golden)
+    H, n, _ = q.shape
+    ref = golden["attn_ref"]
+    assert ref.shape == (n, H * 128)
+    for h in range(H):
+        got = O.attention_f64(q[h], k[h // (H // k.shape[0])], v[h // (H // k.shape[0])], row_limit=np.arange(n))
+        assert np.allclose(got, ref[:, h * 128:(h + 1) * 128], rtol=1e-6, atol=1e-7), f"head {h}"
