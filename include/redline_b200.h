@@ -167,12 +167,14 @@ int rl_swiglu_mlp(const void* x, int x_dtype, int x_quantized, int64_t M, int64_
  * device memory - a serving process that reserves its whole memory pool at start-up and treats any later
  * allocation as a failure, or a latency-critical path where cudaMalloc / cudaFree would synchronise the device.
  * Its scratch is a fixed 32 MiB device array inside this library (rl_swiglu_mlp_noalloc_capacity()), which every
- * GPU that loads the library holds until the process exits; requests needing more
- * (rl_swiglu_mlp_workspace(M, K, F, x_quantized) > 32 MiB) return RL_ERR_ARGUMENT. The call allocates nothing.
+ * GPU that loads the library holds until the process exits. The array must hold the quantised x (M x K bf16,
+ * unless x_quantized) and H (M x F bf16), each rounded up to 256 bytes; requests whose two exceed 32 MiB return
+ * RL_ERR_ARGUMENT. The down GEMM's split-K partials are used only when they fit in the rest of the array too
+ * (otherwise it runs unsplit, with the same results up to fp32 summation order). The call allocates nothing.
  * The first call on each device looks up the array's device address (once, with that device current), so make
- * that first call before any stream capture. All calls share the one array: calls that overlap on the GPU (e.g. on
- * two streams) race on it. Nothing in it needs to start zeroed - each call overwrites everything it reads.
- * Arguments as rl_swiglu_mlp.
+ * that first call before any stream capture; a cudaDeviceReset while the library is loaded invalidates that address
+ * and is not supported. All calls share the one array: calls that overlap on the GPU (e.g. on two streams) race on
+ * it. Nothing in it needs to start zeroed - each call writes everything it reads. Arguments as rl_swiglu_mlp.
  */
 size_t rl_swiglu_mlp_noalloc_capacity(void);
 int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M, int64_t K, const uint8_t* w_up,

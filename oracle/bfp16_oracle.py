@@ -12,6 +12,8 @@ float32 exponent field in the block) followed by 8 signed int8 mantissas, 9 byte
 value = mantissa * 2**(E - 133).
 """
 
+import functools
+
 import numpy as np
 
 BLOCK = 8          # values per bfp16 block
@@ -102,6 +104,7 @@ def quantize_rows(x):
 # stream layouts: redline/npu_layouts.py:11-60, as explicit index maps (element (r, c) -> stream position)
 # ----------------------------------------------------------------------------------------------------------------
 
+@functools.lru_cache(maxsize=8)
 def a_layout_index(M, K, m=128, k=64):
     """Stream position of every (r, c) of an (M, K) A operand: npu_layouts.py:18-23 `a_layout` (L1 tiles m x k
     row-major; inside, 16-row bands, then 8-column blocks, then the band's two 8-row halves, then 8x8 row-major).
@@ -110,9 +113,10 @@ def a_layout_index(M, K, m=128, k=64):
     c = np.arange(K)[None, :]
     tile = (r // m) * (K // k) + c // k
     inner = ((((r % m) // 16) * (k // 8) + (c % k) // 8) * 2 + (r % 16) // 8) * 64 + (r % 8) * 8 + c % 8
-    return tile * (m * k) + inner
+    return _frozen(tile * (m * k) + inner)
 
 
+@functools.lru_cache(maxsize=8)
 def b_layout_index(K, N, k=64, n=128):
     """Stream position of every (r, c) of a (K, N) B operand: npu_layouts.py:11-16 `b_layout` (L1 tiles k x n,
     N-tile outer and K-tile inner; inside, 16-column bands, 8-row blocks, the band's two 8-column halves, then
@@ -121,9 +125,10 @@ def b_layout_index(K, N, k=64, n=128):
     c = np.arange(N)[None, :]
     tile = (c // n) * (K // k) + r // k
     inner = ((((c % n) // 16) * (k // 8) + (r % k) // 8) * 2 + (c % 16) // 8) * 64 + (c % 8) * 8 + r % 8
-    return tile * (k * n) + inner
+    return _frozen(tile * (k * n) + inner)
 
 
+@functools.lru_cache(maxsize=8)
 def c_atb_index(M, N, m=128, n=128, rows=4, cols=8):
     """Stream position of every (r, c) of the (M, N) C the ATB GEMM designs emit: npu_layouts.py:31-48
     `c_layout_atb` (groups of rows x cols tiles, row-group outer; per group one chunk per core column stacking that
@@ -135,7 +140,13 @@ def c_atb_index(M, N, m=128, n=128, rows=4, cols=8):
     i = (rg * (N // (cols * n)) + cg) * cols + col
     for d, v in ((rows, row), (m // 16, sbr), (n // 16, sbc), (2, br), (2, bc), (8, rib), (8, cib)):
         i = i * d + v
-    return i
+    return _frozen(i)
+
+
+def _frozen(idx):
+    """Index maps are cached per shape (the CPU baseline applies the same maps every step), so they are read-only."""
+    idx.setflags(write=False)
+    return idx
 
 
 def _scatter(a, idx):

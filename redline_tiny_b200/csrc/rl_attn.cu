@@ -328,8 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BKV / 2; ++c) {
           const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), scl, nm));
           const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), scl, nm));
-          ls[c & 7] += p0 + p1;
           pk[c] = pack_bf16x2(p0, p1);
+          // the row sum adds the bf16 P that the P.V product multiplies (see softmax_block)
+          ls[c & 7] += __uint_as_float(pk[c] << 16) + __uint_as_float(pk[c] & 0xFFFF0000u);
         }
       }
       l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
@@ -441,8 +442,11 @@ __device__ __forceinline__ void softmax_block(uint32_t ta, uint32_t to, int64_t 
         const int i = 64 * hh + 2 * c;
         const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])), sc2, nm2);
         const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        acc[c & 3] = __fadd2_rn(acc[c & 3], e);
         pk[c] = pack_bf16x2(e.x, e.y);
+        // the row sum adds the bf16 P that the P.V product multiplies, so that O / l weights V by exactly the
+        // normalised P (a sum of the unrounded P would leave up to 2^-9 relative error in O where one key dominates)
+        acc[c & 3] = __fadd2_rn(acc[c & 3], make_float2(__uint_as_float(pk[c] << 16),
+                                                        __uint_as_float(pk[c] & 0xFFFF0000u)));
       }
     }
     RL_TMEM_ST32(ta + 32 * hh, pk);

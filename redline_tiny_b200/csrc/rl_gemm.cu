@@ -78,6 +78,7 @@ struct Params {
   int num_x_tiles, num_w_tiles, num_tiles, KT;
   int splits;            // pair kernel: K split into this many ranges, fp32 partials split_stride elements apart
   int64_t split_stride;
+  int group_x = 0;       // pair kernel tile order: groups of group_x activation tiles (0: one group; pair_tile_coords)
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
   // Convolution (implicit GEMM) when conv_W > 0: the A rows are the pixels of an (H, W, C) image (W % 128 == 0), the
@@ -485,6 +486,20 @@ struct Cfg {
   static_assert(S % G == 0, "the decoder groups must own whole stages");
 };
 
+// Pair tile tt -> (activation tile xt, weight pair wp). Tiles walk groups of p.group_x activation tiles (one group
+// when 0); inside a group the activation tile runs fastest, so the clusters in flight share a few weight pairs and
+// the group's rows of X stay in L2 while every weight pair streams past them once per group.
+__device__ __forceinline__ void pair_tile_coords(const Params& p, int tt, int npairs, int& xt, int& wp) {
+  const int gsz = p.group_x > 0 ? p.group_x : p.num_x_tiles;
+  const int per_group = gsz * npairs;
+  const int g = tt / per_group;
+  const int r = tt - g * per_group;
+  const int x0 = g * gsz;
+  const int gx = min(gsz, p.num_x_tiles - x0);
+  wp = r / gx;
+  xt = x0 + (r - wp * gx);
+}
+
 template <int V, int S, int G, int P>
 __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bfp16_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
@@ -543,7 +558,9 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       bool ok = true;
       for (int t = cid; ok && t < nitems; t += ncl) {
         const int tt = t % ntiles, kt0 = (t / ntiles) * KTs;
-        const int xt = tt % p.num_x_tiles, wt = 2 * (tt / p.num_x_tiles) + static_cast<int>(rank);
+        int xt, wp;
+        pair_tile_coords(p, tt, npairs, xt, wp);
+        const int wt = 2 * wp + static_cast<int>(rank);
         const uint8_t* wsrc = p.w9 + static_cast<int64_t>(wt) * KT * W9_BYTES;
         for (int kt = kt0; kt < kt0 + KTs; ++kt, ++kiter) {
           const int s = kiter % S;
@@ -662,7 +679,9 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     for (int t = cid; ok && t < nitems; t += ncl, ++it) {
       const int tt = t % ntiles;
       const int64_t out_off = static_cast<int64_t>(t / ntiles) * p.split_stride;
-      const int xt = tt % p.num_x_tiles, wt = 2 * (tt / p.num_x_tiles) + static_cast<int>(rank);
+      int xt, wp;
+      pair_tile_coords(p, tt, npairs, xt, wp);
+      const int wt = 2 * wp + static_cast<int>(rank);
       const int b = C::kAccBufs == 2 ? (it & 1) : 0, use = C::kAccBufs == 2 ? (it >> 1) : it;
       float bias_v = 0.0f;
       if (p.bias) {
@@ -859,6 +878,17 @@ int dispatch(int code, const uint16_t* x, const Params& p, cudaStream_t stream) 
   return fail(RL_ERR_ARGUMENT, "rl_linear_bfp16: unknown kernel variant %d", code);
 }
 
+// Activation tiles per group of the pair kernel's tile order (pair_tile_coords): groups hold ~40 MB of X, a third of
+// the 126 MB L2, and are balanced in size. Every group streams all the weights once, and the clusters in flight read
+// the group's X from L2 instead of re-reading X from HBM for every weight pair (M 17408 x K 3072: X alone is 107 MB;
+// measured 965 us per launch in groups against 1138 us in one group).
+inline int group_tiles(int num_x_tiles, int64_t K) {
+  const int64_t gmax = (static_cast<int64_t>(40) << 20) / (static_cast<int64_t>(BN) * K * 2);
+  const int64_t cap = gmax < 1 ? 1 : gmax;
+  const int64_t groups = (num_x_tiles + cap - 1) / cap;
+  return static_cast<int>((num_x_tiles + groups - 1) / groups);
+}
+
 // Split-K for the pair kernel on a grid that would not fill the GPU: the largest S in {2, 4} with S x (pair tiles)
 // <= the pair kernel's resident clusters (one pair of SMs each), KT % S == 0 and at least 16 K steps per split; 1
 // when no split helps (or no device answers the occupancy query).
@@ -944,6 +974,7 @@ int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w
   p.num_w_tiles = static_cast<int>(N / BM);
   p.num_tiles = p.num_x_tiles * p.num_w_tiles;
   p.KT = static_cast<int>(K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, K);
   p.splits = choose_splits(M, K, N);
   p.split_stride = M * N;
   int st = launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
@@ -1008,6 +1039,7 @@ int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_
   p.num_w_tiles = static_cast<int>(N / BM);
   p.num_tiles = p.num_x_tiles * p.num_w_tiles;
   p.KT = static_cast<int>(K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, K);
   p.splits = 1;
   p.split_stride = 0;
   p.mirror = mirror;
@@ -1043,6 +1075,7 @@ int linear_conv(const uint16_t* x, int H, int W, int C, int taps, const uint8_t*
   p.num_w_tiles = static_cast<int>(N / BM);
   p.num_tiles = p.num_x_tiles * p.num_w_tiles;
   p.KT = static_cast<int>(p.K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, p.K);
   p.splits = 1;
   p.split_stride = 0;
   p.conv_W = W;
@@ -1169,6 +1202,10 @@ int rl_swiglu_mlp_noalloc(const void* x, int x_dtype, int x_quantized, int64_t M
                           rl_stream_t stream) {
   using namespace rl;
   RL_REQUIRE(M >= 0 && K > 0 && F2 > 0 && N > 0, RL_ERR_ARGUMENT, "rl_swiglu_mlp_noalloc: bad shape");
+  // bound the sizes before multiplying them, so that the byte count below cannot wrap
+  RL_REQUIRE(M < (int64_t(1) << 31) && K <= (int64_t(1) << 31) && F2 <= (int64_t(1) << 31), RL_ERR_ARGUMENT,
+             "rl_swiglu_mlp_noalloc: size too large (M=%lld K=%lld 2F=%lld)", (long long)M, (long long)K,
+             (long long)F2);
   const size_t need = mlp::base_bytes(M, K, F2 / 2, x_quantized);   // the split-K partials are optional
   RL_REQUIRE(need <= mlp::kStaticScratchBytes, RL_ERR_ARGUMENT,
              "rl_swiglu_mlp_noalloc: M=%lld K=%lld F=%lld needs %zu bytes of scratch, more than the fixed %zu bytes "

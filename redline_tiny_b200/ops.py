@@ -128,9 +128,22 @@ def weights_shard(K, N, rank, world):
     return tuple(x.value for x in v)
 
 
-def linear_bfp16(x_dq, w, bias=None, out=None, out_dtype=torch.bfloat16):
-    """C = x_dq @ B (+ bias), x_dq = bf16 (M, K) holding bfp16 values (quantize_bfp16's decoded output)."""
-    _check_cuda(x_dq, w.native, bias, out)
+def gemm_workspace(M, K, N, device, workspace=None, epilogue=L.RL_EPI_NONE):
+    """A device workspace for the GEMM's split-K schedule (rl_linear_bfp16_workspace bytes; None when the shape does
+    not split). A given workspace that is large enough is reused."""
+    need = L.lib().rl_linear_bfp16_workspace(int(M), int(K), int(N), int(epilogue))
+    if need == 0:
+        return None
+    if workspace is not None and workspace.numel() >= need:
+        return workspace
+    return torch.empty(need, dtype=torch.uint8, device=device)
+
+
+def linear_bfp16(x_dq, w, bias=None, out=None, out_dtype=torch.bfloat16, workspace=None):
+    """C = x_dq @ B (+ bias), x_dq = bf16 (M, K) holding bfp16 values (quantize_bfp16's decoded output). Shapes with
+    too few tiles to fill the GPU and a long K run split-K through a workspace (`workspace`, else one from torch's
+    allocator)."""
+    _check_cuda(x_dq, w.native, bias, out, workspace)
     if x_dq.dtype != torch.bfloat16:
         raise ValueError("x must be bf16 holding bfp16-exact values (quantize_bfp16 decoded output)")
     M, K = x_dq.shape
@@ -139,8 +152,9 @@ def linear_bfp16(x_dq, w, bias=None, out=None, out_dtype=torch.bfloat16):
     if out is None:
         out = torch.empty((M, w.N), dtype=out_dtype, device=x_dq.device)
     epi = L.RL_EPI_BIAS if bias is not None else L.RL_EPI_NONE
-    L.call("rl_linear_bfp16", _ptr(x_dq), M, K, _ptr(w.native), w.N, _ptr(bias), epi, _ptr(out),
-           _dtype_code(out), _stream())
+    ws = gemm_workspace(M, K, w.N, x_dq.device, workspace, epi)
+    L.call("rl_linear_bfp16_ws", _ptr(x_dq), M, K, _ptr(w.native), w.N, _ptr(bias), epi, _ptr(out),
+           _dtype_code(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream())
     return out
 
 

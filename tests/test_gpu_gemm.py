@@ -171,6 +171,28 @@ def test_linear_split_k_small_grid(env):
     assert torch.equal(c, ops.linear_bfp16(dq, w, bias=bt, out_dtype=torch.float32))
 
 
+def test_linear_grouped_tile_order(env):
+    """Pair tiles walk groups of activation tiles sized to ~40 MB of X: at K = 12288 a group is 6 tiles at most, so
+    19 activation tiles (ragged M) form groups of 5, 5, 5 and 4; every tile is computed once and correctly (oracle
+    on rows of every group)."""
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    M, K, N = 4800, 12288, 512
+    x, W, b = _case(M, K, N, seed=31)
+    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+    w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
+    bt = torch.from_numpy(b).to(dev).to(torch.bfloat16)
+    c = torch.empty((M, N), dtype=torch.float32, device=dev)
+    L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
+           c.data_ptr(), L.RL_F32, torch.cuda.current_stream().cuda_stream)
+    ops.device_status()
+    rows = np.unique(np.r_[0:4, 1275:1285, 2555:2565, 3835:3845, 4790:4800])
+    _, xd = O.quantize_rows(x[rows])
+    ref = O.linear(xd, O.unpack_b(O.pack_b(W), K, N), b)
+    err = O.max_rel(c.cpu().numpy()[rows], ref)
+    assert err <= 1e-4, f"max-rel {err:.3e}"
+
+
 @pytest.mark.parametrize("N", [3072, 384])   # the pair kernel and the 1-SM kernel
 def test_linear_mirror_stores_identical_copy(env, N):
     """rl_linear_bfp16_mirror: the output and its mirror (here a second local buffer) both equal rl_linear_bfp16's
@@ -186,7 +208,9 @@ def test_linear_mirror_stores_identical_copy(env, N):
     mir = torch.full((M, N), 5.0, dtype=torch.bfloat16, device=dev)
     L.call("rl_linear_bfp16_mirror", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE, out.data_ptr(),
            mir.data_ptr(), L.RL_BF16, s)
-    ref = ops.linear_bfp16(dq, w)
+    ref = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE, ref.data_ptr(),
+           L.RL_BF16, s)
     ops.device_status()
     assert torch.equal(out, ref) and torch.equal(mir, ref)
     with pytest.raises(L.RedlineError):
@@ -197,11 +221,14 @@ def test_linear_mirror_stores_identical_copy(env, N):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_n_sharded_gemm_equals_unsharded_columns(env, world):
     """The N-split standalone GEMM (each GPU streams the contiguous bytes of its N / world weight columns and computes
-    C[:, its columns], no collective): every shard's output equals the unsharded GEMM's columns bit for bit, at
-    config 1's full size (X[4352, 3072] @ W[3072, 12288] + bias, bf16 out), both from the native tiles and from the
-    reference's own pack_b bytes cut at rl_weights_shard's offsets. The shards run one after another on one GPU: the
-    split needs no peer, so this is the multi-GPU path's arithmetic; the oracle checks sampled rows of each shard."""
+    C[:, its columns], no collective): with whole tiles every shard's output equals the unsharded GEMM's columns bit
+    for bit, at config 1's full size (X[4352, 3072] @ W[3072, 12288] + bias, bf16 out), both from the native tiles
+    and from the reference's own pack_b bytes cut at rl_weights_shard's offsets; through ops.linear_bfp16 (which
+    may take the split-K schedule) it agrees up to fp32 summation order and passes the oracle on sampled rows. The
+    shards run one after another on one GPU: the split needs no peer, so this is the multi-GPU path's
+    arithmetic."""
     torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
     x, W, b = _case(4352, 3072, 12288, seed=21)
     M, K = x.shape
     N = W.shape[1]
@@ -209,7 +236,14 @@ def test_n_sharded_gemm_equals_unsharded_columns(env, world):
     packed = torch.from_numpy(O.pack_b(W)).to(dev)
     w = ops.PackedWeight.from_pack_b(packed, K, N)
     bt = torch.from_numpy(b).to(dev).to(torch.bfloat16)
-    full = ops.linear_bfp16(dq, w, bias=bt)
+    s = torch.cuda.current_stream().cuda_stream
+
+    def whole_tiles(wt, bias):
+        out = torch.empty((M, wt.N), dtype=torch.bfloat16, device=dev)
+        L.call("rl_linear_bfp16", dq.data_ptr(), M, K, wt.native.data_ptr(), wt.N, bias.data_ptr(), L.RL_EPI_BIAS,
+               out.data_ptr(), L.RL_BF16, s)
+        return out
+    full = whole_tiles(w, bt)
     rows = np.r_[0:8, 2040:2056, 4344:4352]
     _, xd = O.quantize_rows(x[rows])
     wd = O.unpack_b(O.pack_b(W), K, N)
@@ -219,14 +253,18 @@ def test_n_sharded_gemm_equals_unsharded_columns(env, world):
         n1 = n0 + ws.N
         assert n0 == covered and ws.N == N // world
         covered = n1
-        c = ops.linear_bfp16(dq, ws, bias=bt[n0:n1].contiguous())
+        bs = bt[n0:n1].contiguous()
+        c = whole_tiles(ws, bs)
         _, _, off, count = ops.weights_shard(K, N, r, world)
         wr = ops.PackedWeight.from_pack_b(packed[off:off + count].contiguous(), K, N // world)
-        c2 = ops.linear_bfp16(dq, wr, bias=bt[n0:n1].contiguous())
+        c2 = whole_tiles(wr, bs)
+        csk = ops.linear_bfp16(dq, ws, bias=bs)
         ops.device_status()
         assert torch.equal(c, full[:, n0:n1]), f"shard {r}/{world} differs from the unsharded columns"
         assert torch.equal(c2, c), f"shard {r}/{world} from the reference's pack_b bytes differs"
+        assert (csk.float() - c.float()).abs().max().item() <= 2.0 ** -7 * c.float().abs().max().item()
         ref = O.linear(xd, wd[:, n0:n1], b[n0:n1])
-        err = O.max_rel(c.float().cpu().numpy()[rows], ref)
-        assert err <= BF16_OUT_TOL, f"shard {r}/{world}: max-rel {err:.3e}"
+        for out in (c, csk):
+            err = O.max_rel(out.float().cpu().numpy()[rows], ref)
+            assert err <= BF16_OUT_TOL, f"shard {r}/{world}: max-rel {err:.3e}"
     assert covered == N

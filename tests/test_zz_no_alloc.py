@@ -5,8 +5,9 @@ treats any later allocation as a failure, or a latency-critical path where cudaM
 the device. This entry point keeps its scratch in a fixed array inside the library instead. The test checks it
 against the workspace-taking entry point (rl_swiglu_mlp) on two calls in a row with different inputs - the second
 call finds the first call's data in the shared array - within the MLP tolerance the other tests use (max-rel
-<= 2e-3), and that a request larger than the array is refused. This file is collected last so that a run stopping at
-its first failure has already run every other test; it passes alone in a fresh process too."""
+<= 2e-3), at the array's exact capacity, and that a request larger than the array is refused. This file is collected
+last so that a run stopping at its first failure has already run every other test; it passes alone in a fresh
+process too."""
 
 import ctypes
 
@@ -27,7 +28,15 @@ def _case(M, K, F, N, seed):
     return x, O.interleave_up(wg, wu), wd.T.copy()
 
 
-def test_noalloc_matches_workspace_entry_on_two_calls():
+def _array_bytes(M, K, F):
+    """What the array must hold: the quantised x and H (M x K and M x F bf16), each rounded up to 256 bytes."""
+    r = lambda v: (v + 255) // 256 * 256
+    return r(M * K * 2) + r(M * F * 2)
+
+
+@pytest.mark.parametrize("M", [512, 1024])
+def test_noalloc_matches_workspace_entry_on_two_calls(M):
+    """M = 512 is config 2 (16.8 MB of the 32 MiB array); M = 1024 fills the array exactly."""
     import torch
     from redline_tiny_b200 import _lib as L
     from redline_tiny_b200 import ops
@@ -35,8 +44,8 @@ def test_noalloc_matches_workspace_entry_on_two_calls():
     lib = L.lib()
     dev = torch.device("cuda:0")
     stream = torch.cuda.current_stream().cuda_stream
-    M, K, F, N = 512, 4096, 12288, 4096          # config 2: needs 16.8 MB of the 32 MiB array
-    assert lib.rl_swiglu_mlp_workspace(M, K, F, 0) <= lib.rl_swiglu_mlp_noalloc_capacity()
+    K, F, N = 4096, 12288, 4096
+    assert _array_bytes(M, K, F) <= lib.rl_swiglu_mlp_noalloc_capacity()
     _, Bup, Bdown = _case(M, K, F, N, seed=1)
     wu = ops.PackedWeight.from_float(torch.from_numpy(Bup).to(dev), swiglu=True)
     wd = ops.PackedWeight.from_float(torch.from_numpy(Bdown).to(dev))
@@ -61,10 +70,14 @@ def test_noalloc_rejects_oversize_request():
 
     lib = L.lib()
     cap = lib.rl_swiglu_mlp_noalloc_capacity()
-    M, K, F = 4096, 4096, 12288                   # 4096 x (4096 + 12288) x 2 B = 134 MB > 32 MiB
-    assert lib.rl_swiglu_mlp_workspace(M, K, F, 0) > cap
     buf = ctypes.create_string_buffer(64)
-    st = lib.rl_swiglu_mlp_noalloc(ctypes.addressof(buf), L.RL_BF16, 0, M, K, ctypes.addressof(buf), 2 * F,
+    K, F = 4096, 12288
+    for M in (1025, 4096):                          # one row past the capacity; 134 MB
+        assert _array_bytes(M, K, F) > cap
+        st = lib.rl_swiglu_mlp_noalloc(ctypes.addressof(buf), L.RL_BF16, 0, M, K, ctypes.addressof(buf), 2 * F,
+                                       ctypes.addressof(buf), 4096, ctypes.addressof(buf), L.RL_BF16, None)
+        assert st == L.RL_ERR_ARGUMENT
+        assert b"more than the fixed" in lib.rl_last_error()
+    st = lib.rl_swiglu_mlp_noalloc(ctypes.addressof(buf), L.RL_BF16, 0, 1 << 40, K, ctypes.addressof(buf), 2 * F,
                                    ctypes.addressof(buf), 4096, ctypes.addressof(buf), L.RL_BF16, None)
-    assert st == L.RL_ERR_ARGUMENT
-    assert b"more than the fixed" in lib.rl_last_error()
+    assert st == L.RL_ERR_ARGUMENT and b"too large" in lib.rl_last_error()
