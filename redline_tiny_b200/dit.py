@@ -111,17 +111,23 @@ class DiT:
 
     tp = (rank, world, group): tensor-parallel over `world` GPUs with `weights` already sharded by shard_weights;
     the out-projection and down-projection write partial sums that are added up across the group (two reductions per
-    block, the block being two sequential sublayers), and the residual / LayerNorm run replicated. reduce_dtype:
+    block, the block being two sequential sublayers). reduce_dtype:
     "peer" (2 GPUs: the projection GEMM stores its bf16 partial into the other rank's memory as it computes it and
-    the LayerNorm kernel adds the two: tp.PeerReduce), "bf16"
-    (one NCCL all-reduce of the bf16 partials), "fp32" (NCCL, fp32 partials) or "auto" (default: "peer" at 2 GPUs,
-    where the transfer overlaps the GEMM, "bf16" otherwise)."""
+    the LayerNorm kernel adds the two: tp.PeerReduce; residual and LayerNorm replicated),
+    "rs" (NCCL reduce-scatter of the bf16 partials, the residual + LayerNorm on this rank's M / world rows only -
+    the residual stream stays sharded by rows - and an NCCL all-gather of the LayerNorm output, the next GEMM's A
+    operand: the bytes of one all-reduce, and 1 / world of the LayerNorm work),
+    "bf16" (one NCCL all-reduce of the bf16 partials, LayerNorm replicated), "fp32" (NCCL, fp32 partials) or "auto"
+    (default: "peer" at 2 GPUs, where the transfer overlaps the GEMM; "rs" above 2 when M splits evenly; else
+    "bf16")."""
 
     def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto"):
-        if reduce_dtype not in ("auto", "peer", "bf16", "fp32"):
-            raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'bf16' or 'fp32', not {reduce_dtype!r}")
+        if reduce_dtype not in ("auto", "peer", "rs", "bf16", "fp32"):
+            raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'rs', 'bf16' or 'fp32', not {reduce_dtype!r}")
         if reduce_dtype == "auto":
-            reduce_dtype = "peer" if tp and tp[1] == 2 else "bf16"
+            reduce_dtype = "peer" if tp and tp[1] == 2 else ("rs" if tp and cfg.M % tp[1] == 0 else "bf16")
+        if tp and reduce_dtype == "rs" and cfg.M % tp[1]:
+            raise ValueError(f"reduce_dtype 'rs' needs M ({cfg.M}) divisible by the group size {tp[1]}")
         self.reduce_dtype = reduce_dtype if tp else None
         self.reduce_f32 = reduce_dtype == "fp32"
         self.cfg = cfg
@@ -172,7 +178,11 @@ class DiT:
         pad, shapes = HG.joint_layout(np.zeros(cfg.text, bool), n_target=cfg.image, grid=cfg.grid)
         self.rope_cs = torch.from_numpy(HG.rope(pad, shapes)).to(dev).contiguous()     # (M, 64, 2)
         bf = dict(dtype=torch.bfloat16, device=dev)
-        self.x = [torch.empty(M, D, **bf) for _ in range(2)]
+        # "rs": this rank's rows [r0, r0 + rows) of the residual stream and of the reduced branch / LayerNorm output
+        self.rows, self.r0 = (M // world, tp[0] * (M // world)) if tp and reduce_dtype == "rs" else (M, 0)
+        self.x = [torch.empty(self.rows, D, **bf) for _ in range(2)]
+        self.c_sh = torch.empty(self.rows, D, **bf) if self.rows < M else None
+        self.a_sh = torch.empty(self.rows, D, **bf) if self.rows < M else None
         self.emb = torch.empty(M, D, **bf)
         self.a = torch.empty(M, D, **bf)
         self.qkv = torch.empty(M, 3 * H * HEAD_DIM, **bf)
@@ -220,11 +230,13 @@ class DiT:
         L.call("rl_linear_bfp16", x.data_ptr(), M, K, w.native.data_ptr(), w.N, None, epi, dst, out_dtype,
                torch.cuda.current_stream().cuda_stream)
 
-    def _ln(self, x, br, params, xo, y):
+    def _ln(self, x, br, params, xo, y, row0=0):
+        """Residual + LayerNorm of rows [row0, row0 + len(x)) of the sequence (text rows use parameter row 1)."""
         M, D = x.shape
         bdt = L.RL_F32 if (br is not None and br.dtype == torch.float32) else L.RL_BF16
+        split = min(max(self.cfg.text - row0, 0), M)
         L.call("rl_ln_mod", x.data_ptr(), None if br is None else br.data_ptr(), bdt, params.data_ptr(), M, D,
-               self.cfg.text, None if xo is None else xo.data_ptr(), y.data_ptr(), None,
+               split, None if xo is None else xo.data_ptr(), y.data_ptr(), None,
                torch.cuda.current_stream().cuda_stream)
 
     def embed(self, latents, text_states):
@@ -236,11 +248,23 @@ class DiT:
                self.lat_dq.data_ptr(), s)
         self._linear(self.lat_dq, self.img_in, self.emb[cfg.text:])
         self.emb[:cfg.text].copy_(text_states.to(self.dev, torch.bfloat16))
-        self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
+        if self.a_sh is None:
+            self._ln(self.emb, None, self.params["first"], self.x[0], self.a)
+            return
+        import torch.distributed as dist
+        self._ln(self.emb[self.r0:self.r0 + self.rows], None, self.params["first"], self.x[0], self.a_sh, self.r0)
+        dist.all_gather_into_tensor(self.a, self.a_sh, group=self.tp[2])
 
     def _branch_ln(self, x, w, xin, params, xo):
         """The out / down projection followed by the residual + LayerNorm; under tensor parallelism the partial
         projections are summed across the group first (in the LayerNorm kernel itself for reduce_dtype "peer")."""
+        if self.a_sh is not None:       # "rs": reduce-scatter, LayerNorm of this rank's rows, all-gather
+            import torch.distributed as dist
+            self._linear(x, w, self.c)
+            dist.reduce_scatter_tensor(self.c_sh, self.c, group=self.tp[2])
+            self._ln(xin, self.c_sh, params, xo, self.a_sh, self.r0)
+            dist.all_gather_into_tensor(self.a, self.a_sh, group=self.tp[2])
+            return
         if self.peer is None:
             self._ln(xin, self._branch(x, w), params, xo, self.a)
             return

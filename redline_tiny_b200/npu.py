@@ -48,6 +48,8 @@ class Device:
     # -- the reference's interface --------------------------------------------------------------------------------
     def run(self, op, art, args):
         t = time.perf_counter()
+        from .iron import Tensor           # buffers of the aie.iron stand-in: their torch views
+        args = [a.torch() if isinstance(a, Tensor) else a for a in args]
         if art.startswith(("atb3sw", "vlm-upsw")):
             self._up_swiglu(*args)
         elif art.startswith(("atb3", "q-atb3", "vlm-gemm")):

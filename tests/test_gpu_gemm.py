@@ -160,7 +160,9 @@ def test_linear_split_k_small_grid(env):
         c = torch.empty((M, N), dtype=dt, device=dev)
         L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
                c.data_ptr(), code, ws.data_ptr(), need, s)
-        u = ops.linear_bfp16(dq, w, bias=bt, out_dtype=dt)
+        u = torch.empty((M, N), dtype=dt, device=dev)
+        L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
+               u.data_ptr(), code, s)
         ops.device_status()
         got = c.float().cpu().numpy()[rows]
         assert O.max_rel(got, ref) <= tol, _diag(got, ref)
@@ -168,7 +170,10 @@ def test_linear_split_k_small_grid(env):
     c = torch.empty((M, N), dtype=torch.float32, device=dev)
     L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
            c.data_ptr(), L.RL_F32, ws.data_ptr(), need - 16, s)
-    assert torch.equal(c, ops.linear_bfp16(dq, w, bias=bt, out_dtype=torch.float32))
+    unsplit = torch.empty((M, N), dtype=torch.float32, device=dev)
+    L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
+           unsplit.data_ptr(), L.RL_F32, s)
+    assert torch.equal(c, unsplit)
 
 
 def test_linear_grouped_tile_order(env):

@@ -1,5 +1,6 @@
 """Tensor-parallel DiT on 2 GPUs (one process per GPU; the partial projections summed by the LayerNorm kernel over
-peer memory, or by an NCCL all-reduce in bf16 or fp32) against the unsharded CPU oracle: velocity cosine >= 0.999;
+peer memory, by an NCCL reduce-scatter with the LayerNorm on each rank's rows and an all-gather of its output, or by
+an NCCL all-reduce in bf16 or fp32) against the unsharded CPU oracle: velocity cosine >= 0.999;
 the peer sum and NCCL's bf16 all-reduce agree bit for bit at 2 ranks. Needs two GPUs; skipped otherwise.
 
 The bounded wait of the fused kernel is checked on one GPU: a signal pad that no rank writes makes the wait run out,
@@ -54,7 +55,7 @@ def _worker(rank, world, port, q, blocks_cfg, reduce_dtype):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("reduce_dtype", ["peer", "bf16", "fp32"])
+@pytest.mark.parametrize("reduce_dtype", ["peer", "rs", "bf16", "fp32"])
 @pytest.mark.parametrize("blocks_cfg", [dict(hidden=256, heads=2, ffn=512, blocks=2, text=64, image=192, grid=(12, 16)),
                                         dict(blocks=1)])
 def test_tp2_dit_matches_oracle(blocks_cfg, reduce_dtype):
