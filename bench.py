@@ -519,7 +519,7 @@ def measure_configs(dev, stream, ws, rank):
     # random-init blocks
     gp = torch.Generator(device=dev).manual_seed(9)
     sign = torch.randint(0, 2, txt_tp.shape, generator=gp, device=dev).float() * 2 - 1
-    v_pert = model.forward(lat_tp, txt_tp * (1 + sign * 2.0 ** -9), HG.SIGMAS[3])
+    v_pert = model.forward(lat_tp, txt_tp * (1 + sign * 2.0 ** -9), HG.SIGMAS[3]).clone()   # forward returns a view
     floor = _cos(v_pert, model.forward(lat_tp, txt_tp, HG.SIGMAS[3]))
     out["C4_dit_step"]["velocity_cos_under_half_ulp_input_change"] = floor
     del v_pert, sign
@@ -569,8 +569,9 @@ def measure_configs(dev, stream, ws, rank):
     if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1
         import torch.distributed as dist
         # the default reduction (at 2 GPUs the projection GEMM stores its bf16 partial into the other rank's memory
-        # and the LayerNorm kernel adds both; above 2 an NCCL reduce-scatter, the LayerNorm on this rank's rows and an
-        # all-gather of its output), the NCCL all-reduce of the bf16 partials beside it, and of fp32 partials. Parity:
+        # and the LayerNorm kernel adds both; above 2 an NCCL all-reduce of the bf16 partials), the NCCL
+        # reduce-scatter + row-sharded LayerNorm + all-gather, or at 2 GPUs the NCCL all-reduce, beside it, and the
+        # NCCL all-reduce of fp32 partials. Parity:
         # the TP velocity against the unsharded model's on the same weights and inputs. Partials rounded to bf16
         # before they are added move every branch value by up to half a bf16 step, so those modes are held to the
         # unsharded model's own agreement under a half-step input change (velocity_cos_under_half_ulp_input_change,
@@ -580,7 +581,7 @@ def measure_configs(dev, stream, ws, rank):
                  "rs": "NCCL reduce-scatter + LayerNorm on M/N rows + NCCL all-gather",
                  "bf16": "NCCL all-reduce, bf16 (LayerNorm replicated)",
                  "fp32": "NCCL all-reduce, fp32 partials (LayerNorm replicated)"}
-        for mode in ("auto", "bf16", "fp32"):
+        for mode in ("auto", "bf16" if ws == 2 else "rs", "fp32"):
             w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
             tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD),
                                reduce_dtype=mode)
@@ -593,7 +594,7 @@ def measure_configs(dev, stream, ws, rank):
             v_modes[mode] = v
             cos, err = _cos(v, v_ref), _max_rel(v, v_ref)
             worst = _max_over_ranks([-cos, err], dev, ws)
-            key = f"C4_dit_step_tp{ws}" + {"auto": "", "bf16": "_nccl_bf16", "fp32": "_nccl_fp32"}[mode]
+            key = f"C4_dit_step_tp{ws}" + {"auto": "", "bf16": "_nccl_bf16", "rs": "_nccl_rs", "fp32": "_nccl_fp32"}[mode]
             bar = COS_BAR if mode == "fp32" else min(COS_BAR, floor)
             e = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
                  "reductions_per_step": 2 * cfg.blocks,

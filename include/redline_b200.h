@@ -309,7 +309,7 @@ int rl_npu_qkv_tables(const uint16_t* tables, int T, float* rope_cs, float* w_q,
 
 /* Tensor-parallel residual + LayerNorm with the row-split projection's all-reduce fused in (the reference runs on one
  * device; the TP DiT adds the out- and down-projection partials across ranks once per sublayer). Every rank's projection writes its bf16 (M, D)
- * partial into a peer-readable buffer (rl_ipc_alloc); rl_tp_signal stores `epoch` into entry [slot][rank] of every rank's signal pad
+ * partial, in rl_linear_bfp16_partial's chunk layout, into a peer-readable buffer (rl_ipc_alloc); rl_tp_signal stores `epoch` into entry [slot][rank] of every rank's signal pad
  * (pads: device array of W pointers to the pads' bases, each W x nslots uint64, zero before first use);
  * rl_ln_mod_tp (rl_ln_mod's math with the branch = bf16 of the fp32 sum, in rank order, of the W partials `parts`, a
  * device array of W pointers) first waits until this rank's pad (`pad` = its base + slot * W) holds >= epoch for
@@ -328,6 +328,13 @@ int rl_ipc_free(void* ptr);
 int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                            const uint16_t* bias, int epilogue, void* out, void* mirror, int out_dtype,
                            rl_stream_t stream);
+/* The tensor-parallel projection's partial C = x @ B (bf16, no bias) in the partial layout rl_ln_mod_tp reads:
+ * 16-row x 32-column chunks of 512 values (1 KB), chunk (r / 16, c / 32) at element ((r / 16) * N / 32 + c / 32) * 512,
+ * element (r % 16) * 32 + c % 32 inside it. out, and mirror when not NULL (the other rank's buffer), hold
+ * ceil(M / 16) * 16 rows; each chunk goes to the mirror as one 1 KB bulk copy while the GEMM runs (sixteen times
+ * fewer, larger NVLink writes than rl_linear_bfp16_mirror's row segments). */
+int rl_linear_bfp16_partial(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                            uint16_t* out, uint16_t* mirror, rl_stream_t stream);
 int rl_tp_signal(void* const* pads, int W, int rank, int slot, unsigned long long epoch, rl_stream_t stream);
 int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
                  unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D, int64_t row_split,

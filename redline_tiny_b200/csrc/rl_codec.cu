@@ -177,6 +177,33 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const T* __restrict_
   }
 }
 
+// The GEMM's A operand alone (row-major blocks, decoded values only, no bytes): each thread quantises kUnroll blocks
+// per pass, their loads issued together (kUnroll x 16 or 32 bytes in flight per thread instead of one block's), the
+// blocks of a pass kThreads apart so every load and store of a warp stays one contiguous 512-byte run.
+constexpr int kUnroll = 4;
+template <typename T>
+__global__ void __launch_bounds__(kThreads) quantize_dq_kernel(const T* __restrict__ x, uint16_t* __restrict__ dq,
+                                                               int64_t nblocks) {
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads * kUnroll;
+  for (int64_t b0 = static_cast<int64_t>(blockIdx.x) * kThreads * kUnroll + threadIdx.x; b0 < nblocks; b0 += step) {
+    uint32_t b[kUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t ob = b0 + static_cast<int64_t>(u) * kThreads;
+      if (ob < nblocks) load_block<T>(x + ob * 8, b[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t ob = b0 + static_cast<int64_t>(u) * kThreads;
+      if (ob < nblocks) {
+        uint32_t E, lo, hi, w[4];
+        bfp16_quant_block_fast(b[u], E, lo, hi, w);
+        *reinterpret_cast<uint4*>(dq + ob * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
 // bf16 (M, K) in one stream order -> another; the orders keep 8 consecutive columns together, so 16-byte moves.
 __global__ void __launch_bounds__(kThreads) permute_bf16_kernel(const uint16_t* __restrict__ src, int src_layout,
                                                                 uint16_t* __restrict__ dst, int dst_layout, int64_t K,
@@ -347,6 +374,17 @@ int rl_quantize_bfp16(const void* x, int x_dtype, int64_t M, int64_t K, int layo
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_quantize_bfp16: needs an sm_100 device");
   const int64_t nblocks = M * K / 8;
   if (nblocks == 0) return RL_OK;
+  if (!q_out && dq_out && layout == RL_ROWMAJOR) {   // decoded values only (the GEMM's A operand): the unrolled kernel
+    const int g = codec::grid_for((nblocks + codec::kUnroll - 1) / codec::kUnroll);
+    if (x_dtype == RL_F32)
+      codec::quantize_dq_kernel<float><<<g, codec::kThreads, 0, stream>>>(static_cast<const float*>(x), dq_out,
+                                                                          nblocks);
+    else
+      codec::quantize_dq_kernel<uint16_t><<<g, codec::kThreads, 0, stream>>>(static_cast<const uint16_t*>(x),
+                                                                             dq_out, nblocks);
+    RL_TRY_CUDA(cudaGetLastError());
+    return RL_OK;
+  }
   const int grid = codec::grid_for(nblocks);
   if (x_dtype == RL_F32)
     codec::quantize_kernel<float><<<grid, codec::kThreads, 0, stream>>>(static_cast<const float*>(x), K, layout,

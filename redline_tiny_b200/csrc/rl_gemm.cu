@@ -81,6 +81,7 @@ struct Params {
   int group_x = 0;       // pair kernel tile order: groups of group_x activation tiles (0: one group; pair_tile_coords)
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
+  int chunked = 0;         // bf16 output in 16-row x 32-column chunks of 1 KB (the tensor-parallel partial layout)
   // Convolution (implicit GEMM) when conv_W > 0: the A rows are the pixels of an (H, W, C) image (W % 128 == 0), the
   // tensor map is 3-D over (C, W, H), and K step kt covers channels 64 (kt % conv_cpt) .. + 63 of tap kt / conv_cpt
   // (taps in (dy, dx) row-major order, conv_cpt = ceil(C / 64) steps per tap).
@@ -153,6 +154,28 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
     }
     __syncwarp();
     uint16_t* outp = static_cast<uint16_t*>(p.out);
+    if (p.chunked) {
+      // the tensor-parallel partial layout: the staged 16 x 32 chunk is one contiguous KB, chunk (x0 / 16,
+      // column / 32) - written whole here (the buffers hold the last chunk row's padding rows too; chunks wholly
+      // past M are skipped) and, to the mirror, as one 1 KB bulk copy instead of sixteen 64-byte rows
+      if (x0 < p.M) {
+        const int64_t chunk = (x0 >> 4) * (p.N >> 5) + ((static_cast<int64_t>(wt) * BM + 32 * q) >> 5);
+        uint4* dst = reinterpret_cast<uint4*>(outp + chunk * 512);
+        dst[lane] = reinterpret_cast<const uint4*>(s16)[lane];
+        dst[lane + 32] = reinterpret_cast<const uint4*>(s16)[lane + 32];
+        if (p.mirror) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            bulk_store(static_cast<uint16_t*>(p.mirror) + chunk * 512, s16, 1024);
+            bulk_commit();
+            bulk_store_wait_read();
+          }
+        }
+      }
+      __syncwarp();
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int idx = lane + 32 * i, rr = idx >> 2, part = idx & 3;
@@ -1043,6 +1066,41 @@ int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_
   p.splits = 1;
   p.split_stride = 0;
   p.mirror = mirror;
+  return dispatch(g_variant, x, p, stream);
+}
+
+int rl_linear_bfp16_partial(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                            uint16_t* out, uint16_t* mirror, rl_stream_t stream) {
+  using namespace rl;
+  using namespace rl::gemm;
+  RL_REQUIRE(x && w_native && out, RL_ERR_ARGUMENT, "rl_linear_bfp16_partial: NULL pointer");
+  RL_REQUIRE(M >= 0 && K >= 64 && K % 64 == 0 && N >= 128 && N % 128 == 0, RL_ERR_ARGUMENT,
+             "rl_linear_bfp16_partial: need K %% 64 == 0, N %% 128 == 0 (M=%lld K=%lld N=%lld)", (long long)M,
+             (long long)K, (long long)N);
+  RL_REQUIRE(aligned(x, 16) && aligned(w_native, 16) && aligned(out, 16) && aligned(mirror, 16), RL_ERR_ALIGNMENT,
+             "rl_linear_bfp16_partial: x, w_native, out and mirror must be 16-byte aligned");
+  RL_REQUIRE(K <= (int64_t)1 << 31 && M < ((int64_t)1 << 31), RL_ERR_ARGUMENT,
+             "rl_linear_bfp16_partial: size too large");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_linear_bfp16_partial: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  Params p;
+  p.w9 = w_native;
+  p.bias = nullptr;
+  p.out = out;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out_f32 = 0;
+  p.epilogue = RL_EPI_NONE;
+  p.num_x_tiles = static_cast<int>((M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, K);
+  p.splits = 1;
+  p.split_stride = 0;
+  p.mirror = mirror;
+  p.chunked = 1;
   return dispatch(g_variant, x, p, stream);
 }
 

@@ -49,10 +49,13 @@ struct TpBranch {
 __device__ __forceinline__ void load_branch(const void* br, int br_f32, TpBranch tp, int64_t r, int64_t D, int64_t kb,
                                             float (&f)[8]) {
   if (tp.W > 0) {
-    unpack8(*(reinterpret_cast<const uint4*>(tp.parts[0] + r * D) + kb), f);
+    // the partials are in the projection GEMM's chunk layout (rl_linear_bfp16_partial): 16-row x 32-column chunks of
+    // 512 values, chunk (r / 16, column / 32); block kb (columns 8 kb .. 8 kb + 7) is 16 contiguous bytes of it
+    const int64_t off = ((r >> 4) * (D >> 5) + (kb >> 2)) * 512 + (r & 15) * 32 + (kb & 3) * 8;
+    unpack8(*reinterpret_cast<const uint4*>(tp.parts[0] + off), f);
     for (int w = 1; w < tp.W; ++w) {
       float g[8];
-      unpack8(*(reinterpret_cast<const uint4*>(tp.parts[w] + r * D) + kb), g);
+      unpack8(*reinterpret_cast<const uint4*>(tp.parts[w] + off), g);
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] += g[i];
     }

@@ -4,9 +4,9 @@ residual + LayerNorm kernel (which adds the two partials: rl_ln_mod_tp).
 
 The tensor-parallel DiT (the reference itself runs on one device) sums the row-split projections' partial outputs
 across ranks before each residual + LayerNorm (one reduction per sublayer, two per block). Here each rank's projection GEMM writes its bf16
-partial tile by tile both into its own buffer and, over NVLink, into the other rank's (rl_linear_bfp16_mirror; the
-buffers are cudaMalloc allocations shared by CUDA IPC handle, plain peer stores), so the transfer overlaps the GEMM's
-math. A one-thread kernel then stores an epoch number into the other rank's signal pad; the LayerNorm kernel waits
+partial tile by tile both into its own buffer and, over NVLink, into the other rank's (rl_linear_bfp16_partial: the
+partial in 16 x 32 chunks of 1 KB, each sent as one bulk copy; the buffers are cudaMalloc allocations shared by CUDA
+IPC handle, plain peer stores), so the transfer overlaps the GEMM's math. A one-thread kernel then stores an epoch number into the other rank's signal pad; the LayerNorm kernel waits
 for the other rank's epoch (a bounded wait) and reads both partials from local memory. Each rank sends its partial
 once - the bytes a ring all-reduce moves - and no separate collective kernel runs.
 
@@ -14,7 +14,7 @@ The sum is formed in fp32 in rank order and rounded to bf16 before the residual:
 two partials bit for bit.
 
 Buffer layout (per rank, one allocation): [slot 0: partial of rank 0 | of rank 1 | slot 1: same | pads: 2 slots x W
-uint64], partials M x D bf16. The out- and down-projections alternate between the slots; epochs increase by one per
+uint64], partials ceil(M / 16) * 16 x D bf16 in the chunk layout. The out- and down-projections alternate between the slots; epochs increase by one per
 use. A rank stores into a slot again only after its wait on the other slot has passed, which the other rank signals
 after its LayerNorm finished reading the slot. Epochs are kernel arguments, so a CUDA graph of a step would replay
 stale epochs: this path is for eager launches only.
@@ -37,7 +37,7 @@ class PeerReduce:
         if world != 2:
             raise ValueError(f"the peer reduction is built for 2 ranks, not {world}")
         self.rank, self.world, self.M, self.D = rank, world, M, D
-        self.part_bytes = (M * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.part_bytes = ((M + 15) // 16 * 16 * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN   # whole 16-row chunks
         self.slot_bytes = world * self.part_bytes
         self.pad_off = 2 * self.slot_bytes
         total = self.pad_off + (2 * world * 8 + _ALIGN - 1) // _ALIGN * _ALIGN

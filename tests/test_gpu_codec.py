@@ -110,3 +110,23 @@ def test_native_repack_consistent(env, swiglu):
     # same bytes, regrouped: the multiset of (exponent, mantissa) blocks is preserved per tile
     assert a.numel() == K * N // 8 * 9
     ops.device_status()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("M,K", [(4352, 3072), (77, 40), (1, 8)])
+def test_decoded_only_quantiser_equals_full_quantiser(M, K, dtype):
+    """The decoded-only row-major quantiser (the GEMM's A operand; an unrolled kernel of its own) writes exactly the
+    decoded values of the full quantiser (bytes + decoded), whose bytes are bit-exact against the oracle above;
+    ragged block counts included."""
+    import torch
+    from redline_tiny_b200 import ops
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(M + K)
+    x = torch.from_numpy((rng.standard_normal((M, K)) * np.exp2(rng.integers(-20, 20, (M, 1)))).astype(np.float32))
+    x = x.to(dev) if dtype == "f32" else x.to(dev).to(torch.bfloat16)
+    q, dq_full = ops.quantize_bfp16(x)
+    _, dq_only = ops.quantize_bfp16(x, want_bytes=False)
+    ops.device_status()
+    assert torch.equal(dq_only, dq_full)
+    ref = O.from_bfp16(O.to_bfp16(x.float().cpu().numpy().reshape(-1))).astype(np.float32).reshape(M, K)
+    assert np.array_equal(dq_only.float().cpu().numpy(), ref)

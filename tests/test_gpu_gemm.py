@@ -273,3 +273,29 @@ def test_n_sharded_gemm_equals_unsharded_columns(env, world):
             err = O.max_rel(out.float().cpu().numpy()[rows], ref)
             assert err <= BF16_OUT_TOL, f"shard {r}/{world}: max-rel {err:.3e}"
     assert covered == N
+
+
+@pytest.mark.parametrize("M,N", [(4352, 3072), (300, 384), (100, 256)])
+def test_linear_partial_chunk_layout(env, M, N):
+    """rl_linear_bfp16_partial (the tensor-parallel projection's output): out and its mirror hold exactly
+    rl_linear_bfp16's values in 16-row x 32-column chunks of 512 (chunk (r / 16, c / 32), row-major inside), ragged M
+    included (the chunks wholly past M are not written, and the last chunk row's padding rows hold no data of
+    interest); the pair kernel (N % 256 == 0) and the 1-SM kernel."""
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    K = 1536
+    x, W, _ = _case(M, K, N, seed=13, bias=False)
+    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
+    w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
+    s = torch.cuda.current_stream().cuda_stream
+    Mp = (M + 15) // 16 * 16
+    out = torch.full((Mp * N,), 3.0, dtype=torch.bfloat16, device=dev)
+    mir = torch.full((Mp * N,), 5.0, dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16_partial", dq.data_ptr(), M, K, w.native.data_ptr(), N, out.data_ptr(), mir.data_ptr(), s)
+    ref = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE, ref.data_ptr(),
+           L.RL_BF16, s)
+    ops.device_status()
+    for buf in (out, mir):
+        rows = buf.view(Mp // 16, N // 32, 16, 32).permute(0, 2, 1, 3).reshape(Mp, N)
+        assert torch.equal(rows[:M], ref)

@@ -86,10 +86,12 @@ def test_ln_mod_tp_wait_runs_out_cleanly():
     from redline_tiny_b200 import _lib as L
     from redline_tiny_b200 import ops
     dev = torch.device("cuda", 0)
-    M, D = 8, 256
+    M, D = 16, 256
     x = torch.randn(M, D, device=dev).to(torch.bfloat16)
     part = torch.randn(M, D, device=dev).to(torch.bfloat16)
-    parts = torch.tensor([part.data_ptr(), part.data_ptr()], dtype=torch.int64, device=dev)
+    # the partials in the projection GEMM's chunk layout: 16-row x 32-column chunks of 512 values
+    chunked = part.view(M // 16, 16, D // 32, 32).permute(0, 2, 1, 3).contiguous()
+    parts = torch.tensor([chunked.data_ptr(), chunked.data_ptr()], dtype=torch.int64, device=dev)
     pad = torch.zeros(2, dtype=torch.int64, device=dev)
     params = torch.ones(2, 2, D, device=dev).to(torch.bfloat16)
     xo = torch.full((M, D), 7.0, device=dev).to(torch.bfloat16)
