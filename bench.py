@@ -316,7 +316,8 @@ def gemm_parity(dq, W, bias, w_full, w_shard, n0, gemm, stream, ws):
 
 def launch_breakdown(model, fn, stream):
     """Per-launch device time of one call of fn (a DiT step): a CUDA event after every C-ABI call and every NCCL
-    collective. Returns ({entry point: [launches, ms]}, [(launch, us) of block 10])."""
+    collective (the events themselves add a few percent to the step). Returns ({entry point: [launches, ms]},
+    [(launch, us) of block 10])."""
     import torch
     import torch.distributed as dist
     from redline_tiny_b200 import _lib as L
@@ -358,8 +359,9 @@ def launch_breakdown(model, fn, stream):
         t = totals.setdefault(name, [0, 0.0])
         t[0] += 1
         t[1] += us / 1e3
-    starts = [i for i, (name, _) in enumerate(seq) if name == "qkv_post"]
-    block = seq[starts[10] - 1:starts[11] - 1] if len(starts) > 11 else []
+    # a block starts at its QKV projection: qkv_linear (fused), or the linear before qkv_post
+    starts = [i - (2 if seq[i - 1][0] == "qkv_post" else 1) for i, (name, _) in enumerate(seq) if name == "attention"]
+    block = seq[starts[10]:starts[11]] if len(starts) > 11 else []
     return {k: [v[0], round(v[1], 3)] for k, v in totals.items()}, [(k, round(v, 1)) for k, v in block]
 
 
@@ -494,11 +496,10 @@ def measure_configs(dev, stream, ws, rank):
     model.embed(lat, txt)
     b0 = model.blocks[0]
 
-    def sublayer():   # config 3: the joint-attention sublayer
-        model._linear(model.a, b0["qkv"], model.qkv)
-        L.call("rl_qkv_post", model.qkv.data_ptr(), model.rope_cs.data_ptr(), b0["wq"].data_ptr(),
-               b0["wk"].data_ptr(), cfg.M, cfg.heads, model.q.data_ptr(), model.k.data_ptr(), model.vt.data_ptr(),
-               model.ldv, stream.cuda_stream)
+    def sublayer():   # config 3: the joint-attention sublayer (QK-RMSNorm + RoPE in the QKV GEMM's epilogue)
+        L.call("rl_qkv_linear", model.a.data_ptr(), cfg.M, cfg.hidden, b0["qkv"].native.data_ptr(), cfg.heads,
+               cfg.heads, model.rope_cs.data_ptr(), b0["wq"].data_ptr(), b0["wk"].data_ptr(), model.q.data_ptr(),
+               model.k.data_ptr(), model.vt.data_ptr(), model.ldv, stream.cuda_stream)
         L.call("rl_attention", model.q.data_ptr(), model.k.data_ptr(), model.vt.data_ptr(), model.ldv, cfg.heads,
                cfg.M, cfg.M, cfg.M, None, 1.0, model.o.data_ptr(), cfg.hidden, stream.cuda_stream)
         model._linear(model.o, b0["o"], model.c)
@@ -510,6 +511,9 @@ def measure_configs(dev, stream, ws, rank):
     ms = _event_ms(lambda: model.denoise_step(lat, txt, 3), 3, 2, stream)
     out["C4_dit_step"] = {"ms": ms, "TFLOP/s": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
                           "TFLOP_per_step": cfg.flop_per_step() / 1e12, "weights_GB": 5.44}
+    totals, block = launch_breakdown(model, lambda: model.denoise_step(lat, txt, 3), stream)
+    out["C4_dit_step"]["launches_per_step"] = totals
+    out["C4_dit_step"]["block10_us"] = block
     # the tensor-parallel check's reference velocity: this unsharded model on the TP inputs (seeds 7, 8)
     lat_tp = torch.randn((cfg.image, cfg.latent_ch), generator=torch.Generator(device=dev).manual_seed(7), device=dev)
     txt_tp = torch.randn((cfg.text, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(8), device=dev)
@@ -829,7 +833,7 @@ def run_ours(args, ws, rank, local):
 # ------------------------------------------------------------------------------------------------------------------
 
 CASES = ("linear_c1", "quantize_c1", "linear_m17408", "swiglu_mlp_c2", "swiglu_up_c2", "attention_c3", "qkv_post_c3",
-         "ln_mod_c4", "dit_block_c4", "vae_conv_128x1152", "vae_conv_512x288")
+         "qkv_gemm_c4", "qkv_linear_c4", "ln_mod_c4", "dit_block_c4", "vae_conv_128x1152", "vae_conv_512x288")
 
 
 def run_case(case, iters):
@@ -899,7 +903,12 @@ def run_case(case, iters):
                    cfg.M, cfg.M, cfg.M, None, 1.0, model.o.data_ptr(), cfg.hidden, s)
         attention()
         model._linear(model.o, b["o"], model.c)
-        fn = {"attention_c3": attention, "qkv_post_c3": qkv_post,
+        def qkv_linear():
+            L.call("rl_qkv_linear", model.a.data_ptr(), cfg.M, cfg.hidden, b["qkv"].native.data_ptr(), cfg.heads,
+                   cfg.heads, model.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(), model.q.data_ptr(),
+                   model.k.data_ptr(), model.vt.data_ptr(), model.ldv, s)
+        fn = {"attention_c3": attention, "qkv_post_c3": qkv_post, "qkv_linear_c4": qkv_linear,
+              "qkv_gemm_c4": lambda: model._linear(model.a, b["qkv"], model.qkv),
               "ln_mod_c4": lambda: model._ln(model.x[0], model.c, model.params["mlp"], model.x[1], model.a),
               "dit_block_c4": lambda: model.block(0)}[c]
     for _ in range(iters):

@@ -225,6 +225,18 @@ int rl_qkv_post_gqa(const uint16_t* qkv, const float* rope_cs, const float* w_q,
                     int Hkv, uint16_t* q, uint16_t* k, uint16_t* vt, int64_t ldv, rl_stream_t stream);
 
 /*
+ * The QKV projection with rl_qkv_post_gqa in its epilogue: one GEMM launch in place of rl_linear_bfp16 + rl_qkv_post
+ * (forward.py:245-246, the qkv_bfp artifact followed by kernels/glue/qkv_post.cc:112-178; redline/vlm_run.py:407-412
+ * for grouped-query heads). x: (M, K) bf16; w_native: the packed (K, (H + 2 Hkv) * 128) QKV weight (H + 2 Hkv even,
+ * K % 64 == 0). The accumulator of each head is rounded to bf16 (the projection's output dtype) and then normalised,
+ * rotated and stored as rl_qkv_post_gqa stores it: q (H, M, 128), k (Hkv, M, 128), vt (Hkv, 128, ldv) with columns
+ * M..ldv-1 zeroed. ldv % 16 == 0 and M <= ldv <= M rounded up to a multiple of 256. Never splits K.
+ */
+int rl_qkv_linear(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int H, int Hkv,
+                  const float* rope_cs, const float* w_q, const float* w_k, uint16_t* q, uint16_t* k, uint16_t* vt,
+                  int64_t ldv, rl_stream_t stream);
+
+/*
  * a12 - joint text+image flash attention, head_dim 128, on tcgen05. Replaces the attention artifacts
  * (kernels/attn/attn_bfp.cc:846-923, run by forward.py:247, 369, 603) and is checked against the float64 softmax of
  * redline/run_attn.py:203-209 (key-tail mask, run_attn.py:153-155) and run_attn.py:123-126 (per-row key limits).

@@ -48,6 +48,7 @@ SIGNATURES = {
     "rl_ln_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "rl_qkv_post": (_I, [_P, _P, _P, _P, _I64, _I, _P, _P, _P, _I64, _P]),
     "rl_qkv_post_gqa": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _I64, _P]),
+    "rl_qkv_linear": (_I, [_P, _I64, _I64, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I64, _P]),
     "rl_rms_mod": (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "rl_attention_gqa": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),
     "rl_attention_gqa_f32": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P]),

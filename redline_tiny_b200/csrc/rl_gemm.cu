@@ -82,6 +82,18 @@ struct Params {
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
   int chunked = 0;         // bf16 output in 16-row x 32-column chunks of 1 KB (the tensor-parallel partial layout)
+  // QKV projection with QK-RMSNorm + RoPE in the epilogue (qkv_H > 0): the weight tiles are [q heads | k heads |
+  // v heads] of 128 columns each; q / k tiles are RMS-normalised per token over their 128 columns (eps 1e-6), scaled
+  // by w_q / w_k and rotated on adjacent column pairs by rope_cs (M, 64, 2) = (cos, sin), written to q_out / k_out
+  // (heads, M, 128); v tiles are written transposed to vt_out (Hkv, 128, ldv), tokens contiguous.
+  int qkv_H = 0, qkv_Hkv = 0;
+  const float* rope_cs = nullptr;
+  const float* w_q = nullptr;
+  const float* w_k = nullptr;
+  uint16_t* q_out = nullptr;
+  uint16_t* k_out = nullptr;
+  uint16_t* vt_out = nullptr;
+  int64_t ldv = 0;
   // Convolution (implicit GEMM) when conv_W > 0: the A rows are the pixels of an (H, W, C) image (W % 128 == 0), the
   // tensor map is 3-D over (C, W, H), and K step kt covers channels 64 (kt % conv_cpt) .. + 63 of tap kt / conv_cpt
   // (taps in (dy, dx) row-major order, conv_cpt = ceil(C / 64) steps per tap).
@@ -107,9 +119,11 @@ struct Barriers {
   uint64_t accf[2];      // MMA commit: accumulator complete
   uint64_t acce[2];      // epilogue: accumulator drained
   uint64_t drain;        // error path: wait for MMAs in flight
+  uint64_t rms[2];       // QKV epilogue: the 4 epilogue warps of column half h have posted their sums of squares
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 // silu with the fast intrinsics (error ~1e-6 relative, far below the bfp16 step the result is rounded to)
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
@@ -220,6 +234,177 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
   }
 }
 
+// ---- QKV epilogue: QK-RMSNorm + RoPE on the accumulator (restates kernels/glue/qkv_post.cc:112-178 and
+// redline/run_glue.py:27-37 as the separate rl_qkv_post does: inv = 1 / sqrt(sum of squares / 128 + 1e-6), n = x * inv
+// * w, (n0 cos - n1 sin, n0 sin + n1 cos) on columns (2i, 2i + 1)). A 128-column weight tile is one head; the four
+// epilogue warps of a column half each hold 32 of its columns for the same tokens, so they post their per-token
+// sums of squares in their staging buffers and meet on an mbarrier (bounded wait) before any of them normalises.
+// The epilogue staging buffer of a warp: [0, 1024) the bf16 tile of a pass-1 chunk, then 1 / rms of the half's 128
+// tokens in pass 2; [1024, 2048) this warp's 128 per-token sums of squares, two buffers by tile parity (another warp
+// of the half may still read tile t's sums while this one posts tile t + 1's: the accumulator it needs for t + 1 is
+// released only after every warp's pass 1, and tile t + 2 needs every warp's pass 1 of t + 1, after its read of t).
+constexpr int kQkvRstdOff = 0;
+constexpr int kQkvPartOff = 1024;
+static_assert(kQkvPartOff + 2 * 512 <= kEpiStageBytes, "QKV epilogue staging");
+constexpr int kQkvU = 2;            // pass 2: tokens per lane whose loads are in flight together
+
+// The warp-wide sum of v[j] for each of 16 tokens j (a transposing butterfly, 16 shuffles): lanes 2t and 2t + 1
+// return the sum for token t.
+__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 16;
+    const float send = up ? v[i] : v[i + 8], keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 4], keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 4;
+    const float send = up ? v[i] : v[i + 2], keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool up = lane & 2;
+    const float send = up ? v[0] : v[1], keep = up ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// The epilogue of one column half of a QKV tile (8 chunks of 16 tokens x this warp's 32 columns). The accumulator is
+// rounded to bf16 first, as the projection's bf16 output is where the reference's qkv_post starts. Pass 1 reads the
+// accumulator once: the per-token sums of squares, and the bf16 values stored to their final place in q / k; the
+// accumulator goes back to the MMA warp (`release`) right after its last load, so pass 2 overlaps the next tile's
+// main loop. Pass 2 waits for the half's four warps (bounded), and then normalises and rotates this warp's own
+// stores in place (8 consecutive dims = 4 RoPE pairs per 16-byte vector, read back from L2). Returns false when
+// the sums' wait ran out.
+template <typename Release>
+__device__ __forceinline__ bool qkv_half(const Params& p, uint32_t tbase, uint8_t* epi_stage, int ew, int lane, int q,
+                                         int h, int wt, int64_t xb, uint64_t* rms_bar, uint32_t& rms_uses,
+                                         volatile int* abort, Release release) {
+  constexpr int NC = BN / 2 / kChunk;
+  uint8_t* st = epi_stage + ew * kEpiStageBytes;
+  const int H = p.qkv_H, Hkv = p.qkv_Hkv;
+  const int kind = wt < H ? 0 : (wt < H + Hkv ? 1 : 2);            // q, k or v head
+  const int head = wt - (kind == 0 ? 0 : (kind == 1 ? H : H + Hkv));
+  const int dim = 32 * q + lane;
+  uint32_t r[kChunk];
+  if (kind == 2) {   // v: column `dim` of the head, 16 consecutive tokens = 32 contiguous bytes of vt's row
+#pragma unroll 1
+    for (int c = 0; c < NC; ++c) {
+      RL_TMEM_LD16(tbase + c * kChunk, r);
+      tmem_ld_wait_regs(r);
+      if (c == NC - 1) release();
+      const int64_t tok0 = xb + c * kChunk;
+      if (tok0 < p.ldv) {   // rows past M are the zero rows of X: zero values, as the padding wants
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w[i]) : "f"(__uint_as_float(r[2 * i + 1])),
+              "f"(__uint_as_float(r[2 * i])));
+        uint4* dst = reinterpret_cast<uint4*>(p.vt_out + (static_cast<int64_t>(head) * 128 + dim) * p.ldv + tok0);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+    return true;
+  }
+  uint16_t* out = (kind == 0 ? p.q_out : p.k_out) + static_cast<int64_t>(head) * p.M * 128;
+  const int pb = kQkvPartOff + 512 * static_cast<int>(rms_uses & 1u);
+  float* part = reinterpret_cast<float*>(st + pb);
+  uint16_t* s16 = reinterpret_cast<uint16_t*>(st);
+  // pass 1: bf16 values to out (through the staging buffer: 16 tokens x this warp's 64 bytes per chunk), and
+  // per-token sums of squares over this warp's 32 columns into its staging buffer
+#pragma unroll 1
+  for (int c = 0; c < NC; ++c) {
+    RL_TMEM_LD16(tbase + c * kChunk, r);
+    tmem_ld_wait_regs(r);
+    if (c == NC - 1) release();
+    float v[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const uint32_t b = float_to_bf16_bits(__uint_as_float(r[j]));
+      const float x = bf16_bits_to_float(b);
+      v[j] = x * x;
+      s16[j * 32 + lane] = static_cast<uint16_t>(b);
+    }
+    const float ss = warp_sum16(v, lane);
+    if (!(lane & 1)) part[c * kChunk + ((lane >> 1) & 15)] = ss;
+    __syncwarp();
+    const int64_t tok0 = xb + c * kChunk;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = lane + 32 * i, rr = idx >> 2, g = idx & 3;
+      const int64_t tok = tok0 + rr;
+      if (tok < p.M)
+        *reinterpret_cast<uint4*>(out + tok * 128 + 32 * q + g * 8) = reinterpret_cast<const uint4*>(s16 + rr * 32)[g];
+    }
+    __syncwarp();
+  }
+  if (lane == 0) mbar_arrive(&rms_bar[h]);   // release: this warp's sums (and its stores) before the others read
+  if (!mbar_wait(&rms_bar[h], rms_uses & 1u, abort)) return false;
+  ++rms_uses;
+  // 1 / rms of the half's 128 tokens from the four warps' sums (each warp its own copy)
+  float* rstd = reinterpret_cast<float*>(st + kQkvRstdOff);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int tok = lane + 32 * i;
+    float sum = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      sum += reinterpret_cast<const float*>(epi_stage + (4 * h + e) * kEpiStageBytes + pb)[tok];
+    rstd[tok] = 1.0f / sqrtf(sum * (1.0f / 128.0f) + 1e-6f);
+  }
+  __syncwarp();
+  // pass 2: lane (t = lane / 4, g = lane % 4) takes dims 32q + 8g .. + 7 of tokens t, t + 8, ...: n = x * rstd * w,
+  // then (n0 cos - n1 sin, n0 sin + n1 cos) per pair, the expressions of the separate rl_qkv_post kernel
+  const int g = lane & 3, t0 = lane >> 2;
+  const float* wsrc = (kind == 0 ? p.w_q : p.w_k) + 32 * q + 8 * g;
+  const float4 wa = __ldg(reinterpret_cast<const float4*>(wsrc)), wb = __ldg(reinterpret_cast<const float4*>(wsrc) + 1);
+  const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll 1
+  for (int k0 = 0; k0 < BN / 2; k0 += 8 * kQkvU) {   // kQkvU tokens per lane per round, their loads issued together
+    uint4 xv[kQkvU];
+    float4 ca[kQkvU], cb[kQkvU];
+#pragma unroll
+    for (int u = 0; u < kQkvU; ++u) {
+      const int64_t tok = xb + k0 + 8 * u + t0;
+      if (tok < p.M) {
+        xv[u] = __ldcg(reinterpret_cast<const uint4*>(out + tok * 128 + 32 * q + 8 * g));
+        const float4* cs = reinterpret_cast<const float4*>(p.rope_cs + tok * 128 + 32 * q + 8 * g);
+        ca[u] = __ldg(cs);
+        cb[u] = __ldg(cs + 1);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kQkvU; ++u) {
+      const int tl = k0 + 8 * u + t0;
+      const int64_t tok = xb + tl;
+      if (tok < p.M) {
+        const float inv = rstd[tl];
+        const uint32_t xw[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+        const float cc[8] = {ca[u].x, ca[u].y, ca[u].z, ca[u].w, cb[u].x, cb[u].y, cb[u].z, cb[u].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float n0 = __uint_as_float(xw[j] << 16) * inv * w8[2 * j];
+          const float n1 = __uint_as_float(xw[j] & 0xFFFF0000u) * inv * w8[2 * j + 1];
+          const float co = cc[2 * j], si = cc[2 * j + 1];
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[j]) : "f"(n0 * si + n1 * co), "f"(n0 * co - n1 * si));
+        }
+        *reinterpret_cast<uint4*>(out + tok * 128 + 32 * q + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  return true;
+}
+
 // Expander step shared by both kernels: decode this thread's weight column `row` of the 8 / P eight-deep blocks of
 // part `part` of a native W9 tile into bf16 pairs (words[4 * b + i] = K rows 8(part * 8 / P + b) + 2i, +1).
 template <int P>
@@ -285,6 +470,8 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       mbar_init(&bars->acce[b], C::kEpiWarps);
     }
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->rms[0], 4);
+    mbar_init(&bars->rms[1], 4);
     bars->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmap_x);
@@ -523,7 +710,8 @@ __device__ __forceinline__ void pair_tile_coords(const Params& p, int tt, int np
   xt = x0 + (r - wp * gx);
 }
 
-template <int V, int S, int G, int P>
+// E = 1: the QKV epilogue (QK-RMSNorm + RoPE, V transposed; Params::qkv_H) instead of the plain / SwiGLU stores.
+template <int V, int S, int G, int P, int E = 0>
 __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bfp16_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
   using C = Cfg<V, S, G, P>;
@@ -558,6 +746,8 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       mbar_init(&bars->acce[b], 2 * C::kEpiWarps);  // the epilogue warps of both CTAs
     }
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->rms[0], 4);
+    mbar_init(&bars->rms[1], 4);
     bars->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmap_x);
@@ -699,6 +889,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     constexpr int NC = BN / 2 / kChunk;
     int it = 0;
     bool ok = true;
+    uint32_t rms_uses = 0;
     for (int t = cid; ok && t < nitems; t += ncl, ++it) {
       const int tt = t % ntiles;
       const int64_t out_off = static_cast<int64_t>(t / ntiles) * p.split_stride;
@@ -716,6 +907,17 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + b * 256 + h * (BN / 2) + ((32u * q) << 16);
       const int64_t xb = static_cast<int64_t>(xt) * BN + h * (BN / 2);
+      if constexpr (E == 1) {
+        if (!qkv_half(p, tbase, epi_stage, ew, lane, q, h, wt, xb, bars->rms, rms_uses, abort, [&] {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_remote(at_leader(&bars->acce[b]));
+            })) {
+          ok = false;
+          break;
+        }
+        continue;
+      }
       uint32_t ra[kChunk], rb[kChunk];
       RL_TMEM_LD16(tbase, ra);
       tmem_ld_wait_regs(ra);
@@ -806,10 +1008,10 @@ int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
 
 // How many 2-CTA clusters of the pair kernel can be resident at once on the current device (cached per device). A
 // cluster's two CTAs share a GPC, so this depends on the chip's GPC layout, not only on the SM count.
-template <int V, int S, int G, int P>
+template <int V, int S, int G, int P, int E = 0>
 int pair_max_clusters(int* out) {
   using C = pair::Cfg<V, S, G, P>;
-  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P>;
+  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P, E>;
   static int cached[64] = {0};
   int dev = 0;
   RL_TRY_CUDA(cudaGetDevice(&dev));
@@ -838,10 +1040,10 @@ int pair_max_clusters(int* out) {
 
 // Pair kernel: clusters of two CTAs; the grid is as many clusters as can be resident at once (at most one per pair
 // tile), each walking pair tiles with stride = number of clusters.
-template <int V, int S, int G, int P>
+template <int V, int S, int G, int P, int E = 0>
 int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   using C = pair::Cfg<V, S, G, P>;
-  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P>;
+  auto kernel = pair::bfp16_linear_pair_kernel<V, S, G, P, E>;
   CUtensorMap tmap;
   int st = make_a_map(&tmap, x, p, 128);
   if (st != RL_OK) return st;
@@ -857,7 +1059,7 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int max_clusters = 0;
-  int st2 = pair_max_clusters<V, S, G, P>(&max_clusters);
+  int st2 = pair_max_clusters<V, S, G, P, E>(&max_clusters);
   if (st2 != RL_OK) return st2;
   const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2) * p.splits;
   const int nclusters = ntiles < max_clusters ? ntiles : max_clusters;
@@ -1067,6 +1269,52 @@ int rl_linear_bfp16_mirror(const uint16_t* x, int64_t M, int64_t K, const uint8_
   p.split_stride = 0;
   p.mirror = mirror;
   return dispatch(g_variant, x, p, stream);
+}
+
+int rl_qkv_linear(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int H, int Hkv,
+                  const float* rope_cs, const float* w_q, const float* w_k, uint16_t* q, uint16_t* k, uint16_t* vt,
+                  int64_t ldv, rl_stream_t stream) {
+  using namespace rl;
+  using namespace rl::gemm;
+  RL_REQUIRE(x && w_native && rope_cs && w_q && w_k && q && k && vt, RL_ERR_ARGUMENT, "rl_qkv_linear: NULL pointer");
+  RL_REQUIRE(H > 0 && Hkv > 0 && H % Hkv == 0 && (H + 2 * Hkv) % 2 == 0 && M >= 0 && K >= 64 && K % 64 == 0,
+             RL_ERR_ARGUMENT, "rl_qkv_linear: need H, Hkv > 0, H %% Hkv == 0, H + 2 Hkv even, K %% 64 == 0");
+  RL_REQUIRE(ldv >= M && ldv % 16 == 0 && ldv <= (M + BN - 1) / BN * BN, RL_ERR_ARGUMENT,
+             "rl_qkv_linear: need M <= ldv <= M rounded up to 256, ldv %% 16 == 0 (M=%lld ldv=%lld)", (long long)M,
+             (long long)ldv);
+  RL_REQUIRE(aligned(x, 16) && aligned(w_native, 16) && aligned(rope_cs, 16) && aligned(w_q, 16) && aligned(w_k, 16) &&
+                 aligned(q, 16) && aligned(k, 16) && aligned(vt, 16),
+             RL_ERR_ALIGNMENT, "rl_qkv_linear: pointers must be 16-byte aligned");
+  RL_REQUIRE(K <= (int64_t)1 << 31 && M < ((int64_t)1 << 31), RL_ERR_ARGUMENT, "rl_qkv_linear: size too large");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_qkv_linear: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  const int64_t N = static_cast<int64_t>(H + 2 * Hkv) * 128;
+  Params p;
+  p.w9 = w_native;
+  p.bias = nullptr;
+  p.out = q;                  // unused: the QKV epilogue writes q, k and vt
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out_f32 = 0;
+  p.epilogue = RL_EPI_NONE;
+  p.num_x_tiles = static_cast<int>((M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, K);
+  p.splits = 1;
+  p.split_stride = 0;
+  p.qkv_H = H;
+  p.qkv_Hkv = Hkv;
+  p.rope_cs = rope_cs;
+  p.w_q = w_q;
+  p.w_k = w_k;
+  p.q_out = q;
+  p.k_out = k;
+  p.vt_out = vt;
+  p.ldv = ldv;
+  return launch_pair<kTmemA, 8, 2, 2, 1>(x, p, stream);
 }
 
 int rl_linear_bfp16_partial(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,

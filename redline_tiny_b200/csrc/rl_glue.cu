@@ -285,6 +285,17 @@ inline int grid_rows(int64_t units, int per_cta) {
   return static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
 }
 
+// Residual + LayerNorm / RMSNorm launch (rl_ln_mod, rl_rms_mod, rl_ln_mod_tp).
+inline int launch_ln_mod(const uint16_t* x, const void* br, int br_f32, TpBranch tp, const unsigned long long* pad,
+                         int rank, unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D,
+                         int64_t row_split, float eps, int rms, uint16_t* xo, uint16_t* y_dq, uint8_t* y_q,
+                         cudaStream_t stream) {
+  ln_mod_kernel<<<grid_rows(M, kWarps), kThreads, 0, stream>>>(x, br, br_f32, tp, pad, rank, epoch, params, M, D,
+                                                               row_split, eps, rms, xo, y_dq, y_q);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
 }  // namespace glue
 }  // namespace rl
 
@@ -298,11 +309,8 @@ static int norm_mod(const char* fn, int rms, const uint16_t* x, const void* bran
              RL_ERR_ALIGNMENT, "%s: bf16 pointers must be 16-byte aligned", fn);
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "%s: needs an sm_100 device", fn);
   if (M == 0) return RL_OK;
-  glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      x, branch, branch_dtype == RL_F32 ? 1 : 0, glue::TpBranch{nullptr, 0}, nullptr, 0, 0ull, params, M, D, row_split,
-      1e-6f, rms, x_out, y_dq, y_q);
-  RL_TRY_CUDA(cudaGetLastError());
-  return RL_OK;
+  return glue::launch_ln_mod(x, branch, branch_dtype == RL_F32 ? 1 : 0, glue::TpBranch{nullptr, 0}, nullptr, 0, 0ull,
+                             params, M, D, row_split, 1e-6f, rms, x_out, y_dq, y_q, stream);
 }
 }  // namespace rl
 

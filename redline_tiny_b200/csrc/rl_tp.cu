@@ -60,10 +60,8 @@ int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const u
              RL_ERR_ALIGNMENT, "rl_ln_mod_tp: bf16 pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod_tp: needs an sm_100 device");
   if (M == 0) return RL_OK;
-  glue::ln_mod_kernel<<<glue::grid_rows(M, glue::kWarps), glue::kThreads, 0, stream>>>(
-      x, nullptr, 0, glue::TpBranch{parts, W}, pad, rank, epoch, params, M, D, row_split, 1e-6f, 0, x_out, y_dq, y_q);
-  RL_TRY_CUDA(cudaGetLastError());
-  return RL_OK;
+  return glue::launch_ln_mod(x, nullptr, 0, glue::TpBranch{parts, W}, pad, rank, epoch, params, M, D, row_split,
+                             1e-6f, 0, x_out, y_dq, y_q, stream);
 }
 
 // Peer-readable buffers: a plain cudaMalloc allocation shared through a CUDA IPC handle (64 bytes), opened by the

@@ -120,9 +120,11 @@ class DiT:
     "bf16" (one NCCL all-reduce of the bf16 partials, LayerNorm replicated), "fp32" (NCCL, fp32 partials) or "auto"
     (default: "peer" at 2 GPUs, where the transfer overlaps the GEMM; "bf16" above - at 4 GPUs NCCL's all-reduce of
     26.7 MB took ~97 us against ~73 us each for its reduce-scatter and all-gather, which outweighs the LayerNorm work
-    "rs" saves: 22.7 against 23.9 ms per step)."""
+    "rs" saves: 22.7 against 23.9 ms per step).
+    fuse_qkv: QK-RMSNorm + RoPE run in the QKV GEMM's epilogue (rl_qkv_linear, when the local head count is even)
+    instead of rl_qkv_post after the GEMM."""
 
-    def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto"):
+    def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto", fuse_qkv=True):
         if reduce_dtype not in ("auto", "peer", "rs", "bf16", "fp32"):
             raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'rs', 'bf16' or 'fp32', not {reduce_dtype!r}")
         if reduce_dtype == "auto":
@@ -131,6 +133,7 @@ class DiT:
             raise ValueError(f"reduce_dtype 'rs' needs M ({cfg.M}) divisible by the group size {tp[1]}")
         self.reduce_dtype = reduce_dtype if tp else None
         self.reduce_f32 = reduce_dtype == "fp32"
+        self.fuse_qkv = fuse_qkv   # False: the QKV GEMM and rl_qkv_post as two launches (the reference's two steps)
         self.cfg = cfg
         dev = torch.device(device)
         self.dev = dev
@@ -304,9 +307,14 @@ class DiT:
         cfg, b = self.cfg, self.blocks[i]
         s = torch.cuda.current_stream().cuda_stream
         M, H = cfg.M, self.heads_local
-        self._linear(self.a, b["qkv"], self.qkv)
-        L.call("rl_qkv_post", self.qkv.data_ptr(), self.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(),
-               M, H, self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
+        if self.fuse_qkv and H % 2 == 0:   # QK-RMSNorm + RoPE in the QKV GEMM's epilogue (pairs of heads per tile)
+            L.call("rl_qkv_linear", self.a.data_ptr(), M, self.a.shape[1], b["qkv"].native.data_ptr(), H, H,
+                   self.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(), self.q.data_ptr(),
+                   self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
+        else:
+            self._linear(self.a, b["qkv"], self.qkv)
+            L.call("rl_qkv_post", self.qkv.data_ptr(), self.rope_cs.data_ptr(), b["wq"].data_ptr(),
+                   b["wk"].data_ptr(), M, H, self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
         L.call("rl_attention", self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, H, M, M, M, None,
                1.0, self.o.data_ptr(), H * HEAD_DIM, s)
         self._branch_ln(self.o, b["o"], self.x[0], self.params["mlp"], self.x[1])

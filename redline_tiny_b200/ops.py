@@ -222,6 +222,23 @@ def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
     return q, k, vt
 
 
+def qkv_linear(x_dq, w, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
+    """linear_bfp16(x_dq, w) followed by qkv_post in one GEMM launch (the norm and RoPE run in the GEMM's epilogue):
+    w = the packed (K, (H + 2 Hkv) * 128) QKV weight with H + 2 Hkv even. Outputs as qkv_post."""
+    _check_cuda(x_dq, w.native, rope_cs, w_q, w_k)
+    M, K = x_dq.shape
+    hkv = heads if kv_heads is None else int(kv_heads)
+    if w.N != (heads + 2 * hkv) * 128:
+        raise ValueError(f"qkv_linear: weight has {w.N} columns, heads need {(heads + 2 * hkv) * 128}")
+    ldv = ldv or (M + 127) // 128 * 128
+    q = torch.empty((heads, M, 128), dtype=torch.bfloat16, device=x_dq.device)
+    k = torch.empty((hkv, M, 128), dtype=torch.bfloat16, device=x_dq.device)
+    vt = torch.empty((hkv, 128, ldv), dtype=torch.bfloat16, device=x_dq.device)
+    L.call("rl_qkv_linear", _ptr(x_dq), M, K, _ptr(w.native), heads, hkv, _ptr(rope_cs), _ptr(w_q), _ptr(w_k),
+           _ptr(q), _ptr(k), _ptr(vt), ldv, _stream())
+    return q, k, vt
+
+
 def attention(q, k, vt, nkv=None, row_limit=None, scale_log2=None, out=None, ldo=None, out_dtype=torch.bfloat16):
     """Flash attention per head: q (H, Nq, 128), k (Hkv, Nk, 128), vt (Hkv, 128, ldv) bf16 -> o (Nq, ldo) with
     head h at columns 128h..; bf16 rounded to bfp16 along the head dim (the out-projection's A operand), or with

@@ -70,7 +70,7 @@ def rms_params(w):
 class LM:
     """Resident packed weights and preallocated buffers for `cfg.layers` decoder layers over M rows."""
 
-    def __init__(self, cfg, weights, M, device="cuda"):
+    def __init__(self, cfg, weights, M, device="cuda", fuse_qkv=True):
         self.cfg, self.M = cfg, M
         dev = torch.device(device)
         self.dev = dev
@@ -91,6 +91,7 @@ class LM:
         self.a = torch.empty(M, D, **bf)
         self.qkv = torch.empty(M, (H + 2 * Hk) * HEAD_DIM, **bf)
         self.ldv = (M + 127) // 128 * 128
+        self.fuse_qkv = fuse_qkv and (cfg.heads + 2 * cfg.kv_heads) % 2 == 0   # rl_qkv_linear: whole head pairs
         self.q = torch.empty(H, M, HEAD_DIM, **bf)
         self.k = torch.empty(Hk, M, HEAD_DIM, **bf)
         self.vt = torch.zeros(Hk, HEAD_DIM, self.ldv, **bf)
@@ -127,10 +128,15 @@ class LM:
         s = torch.cuda.current_stream().cuda_stream
         x0, x1, x2 = self.x[self.cur], self.x[(self.cur + 1) % 3], self.x[(self.cur + 2) % 3]
         self._rms(x0, self.br, lw["p_in"], x1, self.a)
-        self._linear(self.a, lw["qkv"], self.qkv)
-        L.call("rl_qkv_post_gqa", self.qkv.data_ptr(), self.rope_cs.data_ptr(), lw["wq"].data_ptr(),
-               lw["wk"].data_ptr(), M, cfg.heads, cfg.kv_heads, self.q.data_ptr(), self.k.data_ptr(),
-               self.vt.data_ptr(), self.ldv, s)
+        if self.fuse_qkv:   # QK-RMSNorm + RoPE in the QKV GEMM's epilogue
+            L.call("rl_qkv_linear", self.a.data_ptr(), M, cfg.hidden, lw["qkv"].native.data_ptr(), cfg.heads,
+                   cfg.kv_heads, self.rope_cs.data_ptr(), lw["wq"].data_ptr(), lw["wk"].data_ptr(),
+                   self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)
+        else:
+            self._linear(self.a, lw["qkv"], self.qkv)
+            L.call("rl_qkv_post_gqa", self.qkv.data_ptr(), self.rope_cs.data_ptr(), lw["wq"].data_ptr(),
+                   lw["wk"].data_ptr(), M, cfg.heads, cfg.kv_heads, self.q.data_ptr(), self.k.data_ptr(),
+                   self.vt.data_ptr(), self.ldv, s)
         L.call("rl_attention_gqa", self.q.data_ptr(), self.k.data_ptr(), self.vt.data_ptr(), self.ldv, cfg.heads,
                cfg.kv_heads, M, M, self.valid, self.row_limit.data_ptr(), 1.0, self.o.data_ptr(),
                cfg.heads * HEAD_DIM, s)

@@ -20,12 +20,12 @@ def _cos(a, b):
     return float(a @ b / np.sqrt((a @ a) * (b @ b)))
 
 
-def _check(cfg, sigma_index=1, seed=0):
+def _check(cfg, sigma_index=1, seed=0, fuse_qkv=True):
     import torch
     from redline_tiny_b200 import dit, host_glue as HG, ops
 
     w = dit.random_weights(cfg, seed=seed)
-    model = dit.DiT(cfg, w)
+    model = dit.DiT(cfg, w, fuse_qkv=fuse_qkv)
     rng = np.random.default_rng(seed)
     lat = rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32)
     txt = rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32)
@@ -43,10 +43,12 @@ def _check(cfg, sigma_index=1, seed=0):
     return cv
 
 
-def test_dit_small():
+@pytest.mark.parametrize("fuse_qkv", [True, False])
+def test_dit_small(fuse_qkv):
+    """Both QKV forms: QK-RMSNorm + RoPE in the QKV GEMM's epilogue (rl_qkv_linear) and as rl_qkv_post."""
     from redline_tiny_b200 import dit
     cfg = dit.DiTConfig(hidden=256, heads=2, ffn=512, blocks=2, text=64, image=192, grid=(12, 16))
-    _check(cfg)
+    _check(cfg, fuse_qkv=fuse_qkv)
 
 
 def test_dit_config4_architecture_one_block():

@@ -89,7 +89,8 @@ def _ln_inputs(M, D, seed):
     return O.bf16_round(x), O.quantize_rows(br)[1], g, sc
 
 
-@pytest.mark.parametrize("M,D,split", [(256, 128, 128), (300, 3072, 0), (4352, 3072, 256)])
+@pytest.mark.parametrize("M,D,split", [(256, 128, 128), (300, 3072, 0), (4352, 3072, 256), (100, 1032, 50),
+                                     (200, 4096, 0), (64, 8256, 10)])
 def test_ln_mod(env, golden, M, D, split):
     torch, ops, dev = env
     if M == 256 and D == 128:
@@ -150,3 +151,74 @@ def test_qkv_post(env, golden, M, H):
         v = qkv[:, (2 * H + h) * 128:(2 * H + h + 1) * 128]
         assert np.array_equal(vt[h][:, :M], v.T)
         assert not vt[h][:, M:].any()
+
+
+@pytest.mark.parametrize("M,K,H,Hkv,ldv", [(300, 256, 2, 2, None), (300, 512, 4, 1, 304), (200, 512, 4, 1, 256),
+                                           (1088, 2048, 32, 8, None), (4352, 3072, 24, 24, None)])
+def test_qkv_linear_fused(env, M, K, H, Hkv, ldv):
+    """rl_qkv_linear (QK-RMSNorm + RoPE in the QKV GEMM's epilogue) against the two-launch form it replaces:
+    rl_linear_bfp16 (the same pair kernel, so the same fp32 accumulators) followed by rl_qkv_post_gqa. V is the same
+    bf16 rounding of the same accumulator: bit-exact, zero columns M..ldv-1 included. q / k sum their squares in
+    another order and may contract the RoPE products into FMAs differently, so a value may land one bf16 step away:
+    >= 97% bit-identical, and within 2^-6 of the head's largest |value|; both forms meet the oracle's rms_rope bar
+    of test_qkv_post."""
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    rng = np.random.default_rng(M + 7 * H + Hkv)
+    N = (H + 2 * Hkv) * 128
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
+    _, xdq = ops.quantize_bfp16(x.to(torch.bfloat16), want_bytes=False)
+    W = torch.from_numpy((rng.standard_normal((K, N)) * 0.03).astype(np.float32)).to(dev)
+    w = ops.PackedWeight.from_float(W)
+    ang = rng.uniform(-np.pi, np.pi, (M, 64))
+    cs = np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32)
+    wq = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32) * np.float32(np.log2(np.e) / np.sqrt(128))
+    wk = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    cs_t, wq_t, wk_t = (torch.from_numpy(a).to(dev) for a in (cs, wq, wk))
+    qkv = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16", xdq.data_ptr(), M, K, w.native.data_ptr(), N, None, L.RL_EPI_NONE, qkv.data_ptr(),
+           L.RL_BF16, torch.cuda.current_stream().cuda_stream)
+    q0, k0, vt0 = ops.qkv_post(qkv, cs_t, wq_t, wk_t, H, ldv=ldv, kv_heads=Hkv)
+    vt1 = torch.full_like(vt0, 7.0)           # the fused form must write the padding columns too
+    q1, k1, _ = ops.qkv_linear(xdq, w, cs_t, wq_t, wk_t, H, ldv=ldv, kv_heads=Hkv)
+    L.call("rl_qkv_linear", xdq.data_ptr(), M, K, w.native.data_ptr(), H, Hkv, cs_t.data_ptr(), wq_t.data_ptr(),
+           wk_t.data_ptr(), q1.data_ptr(), k1.data_ptr(), vt1.data_ptr(), vt0.shape[2],
+           torch.cuda.current_stream().cuda_stream)
+    ops.device_status()
+    assert torch.equal(vt1.view(torch.int16), vt0.view(torch.int16))
+    qkv_np = qkv.float().cpu().numpy()
+    for name, a, b in (("q", q1, q0), ("k", k1, k0)):
+        same = (a.view(torch.int16) == b.view(torch.int16)).float().mean().item()
+        assert same >= 0.97, f"{name}: only {same:.4f} of values bit-identical"
+        for hh in range(a.shape[0]):
+            lim = 2.0 ** -6 * b[hh].float().abs().max().item()
+            d = (a[hh].float() - b[hh].float()).abs().max().item()
+            assert d <= lim, f"{name} head {hh}: max |fused - unfused| {d:.3e} > {lim:.3e}"
+    q1n, k1n = q1.float().cpu().numpy(), k1.float().cpu().numpy()
+    for hh in range(min(H, 4)):
+        ref = O.rms_rope(qkv_np[:, hh * 128:(hh + 1) * 128], wq, cs[..., 0], cs[..., 1])
+        err, c = O.max_rel(q1n[hh], ref), O.corr(q1n[hh], ref)
+        assert err <= 8e-3 and c > 0.9999, f"q head {hh}: max-rel {err:.3e} corr {c:.6f}"
+    for hh in range(min(Hkv, 4)):
+        ref = O.rms_rope(qkv_np[:, (H + hh) * 128:(H + hh + 1) * 128], wk, cs[..., 0], cs[..., 1])
+        err, c = O.max_rel(k1n[hh], ref), O.corr(k1n[hh], ref)
+        assert err <= 8e-3 and c > 0.9999, f"k head {hh}: max-rel {err:.3e} corr {c:.6f}"
+
+
+def test_qkv_linear_rejects_bad_shapes(env):
+    torch, ops, dev = env
+    from redline_tiny_b200 import _lib as L
+    x = torch.zeros(64, 128, dtype=torch.bfloat16, device=dev)
+    cs = torch.zeros(64, 64, 2, device=dev)
+    wn = torch.ones(128, device=dev)
+    w3 = ops.PackedWeight.from_float(torch.zeros(128, 3 * 128, device=dev))   # 3 heads: not whole head pairs
+    with pytest.raises(L.RedlineError):
+        ops.qkv_linear(x, w3, cs, wn, wn, 1)
+    w4 = ops.PackedWeight.from_float(torch.zeros(128, 4 * 128, device=dev))   # H 2, Hkv 1
+    with pytest.raises(ValueError):
+        ops.qkv_linear(x, w4, cs, wn, wn, 2)                                  # Hkv 2 would need 6 heads
+    with pytest.raises(L.RedlineError):
+        ops.qkv_linear(x, w4, cs, wn, wn, 2, kv_heads=1, ldv=72)              # ldv % 16 != 0
+    with pytest.raises(L.RedlineError):
+        ops.qkv_linear(x, w4, cs, wn, wn, 2, kv_heads=1, ldv=512)             # past M rounded up to 256
+    ops.device_status()

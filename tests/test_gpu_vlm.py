@@ -103,12 +103,14 @@ def test_attention_gqa_causal(env, H, Hkv, N, valid):
 
 @pytest.mark.parametrize("dims", [dict(hidden=512, heads=4, kv_heads=2, ffn=1024, M=384, valid=300),
                                   dict(hidden=1024, heads=8, kv_heads=2, ffn=2048, M=512, valid=433)])
-def test_lm_layer(env, dims):
+@pytest.mark.parametrize("fuse_qkv", [True, False])
+def test_lm_layer(env, dims, fuse_qkv):
     torch, ops, vlm, dev = env
+    dims = dict(dims)
     M, valid = dims.pop("M"), dims.pop("valid")
     cfg = vlm.LMConfig(**dims, layers=1)
     w = vlm.random_lm_weights(cfg, seed=7)
-    lm = vlm.LM(cfg, w, M)
+    lm = vlm.LM(cfg, w, M, fuse_qkv=fuse_qkv)
     cos, sin = _rope(M, valid)
     lm.set_positions(cos, sin, valid)
     rng = np.random.default_rng(7)
