@@ -82,6 +82,10 @@ struct Params {
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
   int chunked = 0;         // bf16 output in 16-row x 32-column chunks of 1 KB (the tensor-parallel partial layout)
+  // chunked output scattered by rows (the tensor-parallel reduce-scatter): rows [o R, o R + R) go, as whole 1 KB
+  // chunks in the same layout restarted at row o R, to scatter[o] (rank o's receive buffer; peers over NVLink)
+  uint16_t* const* scatter = nullptr;
+  int64_t scatter_rows = 0;
   // QKV projection with QK-RMSNorm + RoPE in the epilogue (qkv_H > 0): the weight tiles are [q heads | k heads |
   // v heads] of 128 columns each; q / k tiles are RMS-normalised per token over their 128 columns (eps 1e-6), scaled
   // by w_q / w_k and rotated on adjacent column pairs by rope_cs (M, 64, 2) = (cos, sin), written to q_out / k_out
@@ -172,6 +176,22 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
       // the tensor-parallel partial layout: the staged 16 x 32 chunk is one contiguous KB, chunk (x0 / 16,
       // column / 32) - written whole here (the buffers hold the last chunk row's padding rows too; chunks wholly
       // past M are skipped) and, to the mirror, as one 1 KB bulk copy instead of sixteen 64-byte rows
+      if (p.scatter) {
+        if (x0 < p.M) {
+          const int64_t o = x0 / p.scatter_rows;
+          const int64_t chunk = ((x0 - o * p.scatter_rows) >> 4) * (p.N >> 5) +
+                                ((static_cast<int64_t>(wt) * BM + 32 * q) >> 5);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            bulk_store(p.scatter[o] + chunk * 512, s16, 1024);
+            bulk_commit();
+            bulk_store_wait_read();
+          }
+        }
+        __syncwarp();
+        return;
+      }
       if (x0 < p.M) {
         const int64_t chunk = (x0 >> 4) * (p.N >> 5) + ((static_cast<int64_t>(wt) * BM + 32 * q) >> 5);
         uint4* dst = reinterpret_cast<uint4*>(outp + chunk * 512);
@@ -1349,6 +1369,45 @@ int rl_linear_bfp16_partial(const uint16_t* x, int64_t M, int64_t K, const uint8
   p.split_stride = 0;
   p.mirror = mirror;
   p.chunked = 1;
+  return dispatch(g_variant, x, p, stream);
+}
+
+int rl_linear_bfp16_scatter(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
+                            uint16_t* const* dsts, int W, int64_t rows_per_rank, rl_stream_t stream) {
+  using namespace rl;
+  using namespace rl::gemm;
+  RL_REQUIRE(x && w_native && dsts && W >= 1 && W <= 64, RL_ERR_ARGUMENT, "rl_linear_bfp16_scatter: bad arguments");
+  RL_REQUIRE(M >= 0 && K >= 64 && K % 64 == 0 && N >= 128 && N % 128 == 0 && rows_per_rank > 0 &&
+                 rows_per_rank % 16 == 0 && M == W * rows_per_rank,
+             RL_ERR_ARGUMENT,
+             "rl_linear_bfp16_scatter: need K %% 64 == 0, N %% 128 == 0, M = W x rows_per_rank, rows_per_rank %% 16 "
+             "== 0 (M=%lld K=%lld N=%lld W=%d)",
+             (long long)M, (long long)K, (long long)N, W);
+  RL_REQUIRE(aligned(x, 16) && aligned(w_native, 16) && aligned(dsts, 8), RL_ERR_ALIGNMENT,
+             "rl_linear_bfp16_scatter: x and w_native must be 16-byte aligned");
+  RL_REQUIRE(K <= (int64_t)1 << 31 && M < ((int64_t)1 << 31), RL_ERR_ARGUMENT,
+             "rl_linear_bfp16_scatter: size too large");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_linear_bfp16_scatter: needs an sm_100 device");
+  if (M == 0) return RL_OK;
+  Params p;
+  p.w9 = w_native;
+  p.bias = nullptr;
+  p.out = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out_f32 = 0;
+  p.epilogue = RL_EPI_NONE;
+  p.num_x_tiles = static_cast<int>((M + BN - 1) / BN);
+  p.num_w_tiles = static_cast<int>(N / BM);
+  p.num_tiles = p.num_x_tiles * p.num_w_tiles;
+  p.KT = static_cast<int>(K / BK);
+  p.group_x = group_tiles(p.num_x_tiles, K);
+  p.splits = 1;
+  p.split_stride = 0;
+  p.chunked = 1;
+  p.scatter = dsts;
+  p.scatter_rows = rows_per_rank;
   return dispatch(g_variant, x, p, stream);
 }
 

@@ -45,6 +45,12 @@ struct TpBranch {
   const uint16_t* const* parts;   // device array of W pointers, or null
   int W;
 };
+// Extra destinations of y (the tensor-parallel all-gather: this rank's rows of the LayerNorm output stored into every
+// rank's copy of the next GEMM's A operand, peers over NVLink): a device array of n row-0 pointers, or n = 0.
+struct YPeers {
+  uint16_t* const* dst;
+  int n;
+};
 
 __device__ __forceinline__ void load_branch(const void* br, int br_f32, TpBranch tp, int64_t r, int64_t D, int64_t kb,
                                             float (&f)[8]) {
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ params, int64_t M, int64_t D,
                                                           int64_t row_split, float eps, int rms,
                                                           uint16_t* __restrict__ xo, uint16_t* __restrict__ y_dq,
-                                                          uint8_t* __restrict__ y_q) {
+                                                          uint8_t* __restrict__ y_q, YPeers yp) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t KB = D >> 3;
   if (tp.W > 0) {
@@ -166,7 +172,9 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
       for (int i = 0; i < 8; ++i) bits[i] = __float_as_uint((v[i] - mean) * rstd * sf[i]);
       uint32_t E, lo, hi, wq[4];
       bfp16_quant_block_fast(bits, E, lo, hi, wq);
-      if (y_dq) reinterpret_cast<uint4*>(y_dq + r * D)[kb] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+      const uint4 yv = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+      if (y_dq) reinterpret_cast<uint4*>(y_dq + r * D)[kb] = yv;
+      for (int i = 0; i < yp.n; ++i) reinterpret_cast<uint4*>(yp.dst[i] + r * D)[kb] = yv;
       if (y_q) {
         uint8_t* dst = y_q + (r * KB + kb) * 9;
         dst[0] = static_cast<uint8_t>(E);
@@ -289,9 +297,9 @@ inline int grid_rows(int64_t units, int per_cta) {
 inline int launch_ln_mod(const uint16_t* x, const void* br, int br_f32, TpBranch tp, const unsigned long long* pad,
                          int rank, unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D,
                          int64_t row_split, float eps, int rms, uint16_t* xo, uint16_t* y_dq, uint8_t* y_q,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, YPeers yp = YPeers{nullptr, 0}) {
   ln_mod_kernel<<<grid_rows(M, kWarps), kThreads, 0, stream>>>(x, br, br_f32, tp, pad, rank, epoch, params, M, D,
-                                                               row_split, eps, rms, xo, y_dq, y_q);
+                                                               row_split, eps, rms, xo, y_dq, y_q, yp);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

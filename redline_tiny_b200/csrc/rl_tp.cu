@@ -34,6 +34,26 @@ __global__ void signal_kernel(unsigned long long* const* pads, int W, int rank, 
   }
 }
 
+// One thread waits (bounded) until every other rank's entry of `pad` has reached `epoch`; the kernels after it on
+// the stream start only when it ends. On timeout it records kErrWaitTimeout and returns.
+__global__ void wait_kernel(const unsigned long long* pad, int W, int rank, unsigned long long epoch) {
+  if (threadIdx.x != 0) return;
+  for (int w = 0; w < W; ++w) {
+    if (w == rank) continue;
+    const long long t0 = clock64();
+    while (true) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pad + w) : "memory");
+      if (v >= epoch) break;
+      if (clock64() - t0 > RL_WAIT_LIMIT_CYCLES) {
+        report(kErrWaitTimeout);
+        return;
+      }
+      __nanosleep(200);
+    }
+  }
+}
+
 }  // namespace tp
 }  // namespace rl
 
@@ -62,6 +82,33 @@ int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const u
   if (M == 0) return RL_OK;
   return glue::launch_ln_mod(x, nullptr, 0, glue::TpBranch{parts, W}, pad, rank, epoch, params, M, D, row_split,
                              1e-6f, 0, x_out, y_dq, y_q, stream);
+}
+
+int rl_tp_wait(const unsigned long long* pad, int W, int rank, unsigned long long epoch, rl_stream_t stream) {
+  using namespace rl;
+  RL_REQUIRE(pad && W >= 1 && W <= 64 && rank >= 0 && rank < W && epoch > 0 && aligned(pad, 8), RL_ERR_ARGUMENT,
+             "rl_tp_wait: bad arguments");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_tp_wait: needs an sm_100 device");
+  tp::wait_kernel<<<1, 32, 0, stream>>>(pad, W, rank, epoch);
+  RL_TRY_CUDA(cudaGetLastError());
+  return RL_OK;
+}
+
+int rl_ln_mod_tp_rs(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
+                    unsigned long long epoch, const uint16_t* params, int64_t R, int64_t D, int64_t row_split,
+                    uint16_t* x_out, uint16_t* const* y_dsts, rl_stream_t stream) {
+  using namespace rl;
+  RL_REQUIRE(x && parts && pad && params && x_out && y_dsts && W >= 1 && W <= 64 && rank >= 0 && rank < W &&
+                 epoch > 0,
+             RL_ERR_ARGUMENT, "rl_ln_mod_tp_rs: bad arguments");
+  RL_REQUIRE(R >= 0 && R % 16 == 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT,
+             "rl_ln_mod_tp_rs: need R %% 16 == 0 and D %% 8 == 0");
+  RL_REQUIRE(aligned(x, 16) && aligned(params, 16) && aligned(x_out, 16) && aligned(pad, 8) && aligned(y_dsts, 8),
+             RL_ERR_ALIGNMENT, "rl_ln_mod_tp_rs: bf16 pointers must be 16-byte aligned");
+  RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod_tp_rs: needs an sm_100 device");
+  if (R == 0) return RL_OK;
+  return glue::launch_ln_mod(x, nullptr, 0, glue::TpBranch{parts, W}, pad, rank, epoch, params, R, D, row_split,
+                             1e-6f, 0, x_out, nullptr, nullptr, stream, glue::YPeers{y_dsts, W});
 }
 
 // Peer-readable buffers: a plain cudaMalloc allocation shared through a CUDA IPC handle (64 bytes), opened by the

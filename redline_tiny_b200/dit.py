@@ -117,6 +117,9 @@ class DiT:
     "rs" (NCCL reduce-scatter of the bf16 partials, the residual + LayerNorm on this rank's M / world rows only -
     the residual stream stays sharded by rows - and an NCCL all-gather of the LayerNorm output, the next GEMM's A
     operand: the bytes of one all-reduce, and 1 / world of the LayerNorm work),
+    "peer_rs" (the same three steps over peer memory on any number of GPUs: the projection GEMM stores each row
+    block of its partial straight into the owning rank's memory as it computes it, the LayerNorm kernel of the owner
+    adds the partials of its rows and stores its rows of the output into every rank's A operand: tp.PeerRS),
     "bf16" (one NCCL all-reduce of the bf16 partials, LayerNorm replicated), "fp32" (NCCL, fp32 partials) or "auto"
     (default: "peer" at 2 GPUs, where the transfer overlaps the GEMM; "bf16" above - at 4 GPUs NCCL's all-reduce of
     26.7 MB took ~97 us against ~73 us each for its reduce-scatter and all-gather, which outweighs the LayerNorm work
@@ -125,12 +128,16 @@ class DiT:
     instead of rl_qkv_post after the GEMM."""
 
     def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto", fuse_qkv=True):
-        if reduce_dtype not in ("auto", "peer", "rs", "bf16", "fp32"):
-            raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'rs', 'bf16' or 'fp32', not {reduce_dtype!r}")
+        if reduce_dtype not in ("auto", "peer", "peer_rs", "rs", "bf16", "fp32"):
+            raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'peer_rs', 'rs', 'bf16' or 'fp32', "
+                             f"not {reduce_dtype!r}")
         if reduce_dtype == "auto":
             reduce_dtype = "peer" if tp and tp[1] == 2 else "bf16"
         if tp and reduce_dtype == "rs" and cfg.M % tp[1]:
             raise ValueError(f"reduce_dtype 'rs' needs M ({cfg.M}) divisible by the group size {tp[1]}")
+        if tp and reduce_dtype == "peer_rs" and (cfg.M % tp[1] or (cfg.M // tp[1]) % 16):
+            raise ValueError(f"reduce_dtype 'peer_rs' needs M / group size ({cfg.M} / {tp[1]}) to be a multiple "
+                             f"of 16")
         self.reduce_dtype = reduce_dtype if tp else None
         self.reduce_f32 = reduce_dtype == "fp32"
         self.fuse_qkv = fuse_qkv   # False: the QKV GEMM and rl_qkv_post as two launches (the reference's two steps)
@@ -182,10 +189,12 @@ class DiT:
         pad, shapes = HG.joint_layout(np.zeros(cfg.text, bool), n_target=cfg.image, grid=cfg.grid)
         self.rope_cs = torch.from_numpy(HG.rope(pad, shapes)).to(dev).contiguous()     # (M, 64, 2)
         bf = dict(dtype=torch.bfloat16, device=dev)
-        # "rs": this rank's rows [r0, r0 + rows) of the residual stream and of the reduced branch / LayerNorm output
-        self.rows, self.r0 = (M // world, tp[0] * (M // world)) if tp and reduce_dtype == "rs" else (M, 0)
+        # "rs" / "peer_rs": this rank's rows [r0, r0 + rows) of the residual stream and of the reduced branch /
+        # LayerNorm output
+        sharded = bool(tp) and reduce_dtype in ("rs", "peer_rs")
+        self.rows, self.r0 = (M // world, tp[0] * (M // world)) if sharded else (M, 0)
         self.x = [torch.empty(self.rows, D, **bf) for _ in range(2)]
-        self.c_sh = torch.empty(self.rows, D, **bf) if self.rows < M else None
+        self.c_sh = torch.empty(self.rows, D, **bf) if self.rows < M and reduce_dtype == "rs" else None
         self.a_sh = torch.empty(self.rows, D, **bf) if self.rows < M else None
         self.emb = torch.empty(M, D, **bf)
         self.a = torch.empty(M, D, **bf)
@@ -201,10 +210,14 @@ class DiT:
         self.lat_dq = torch.empty(cfg.image, cfg.latent_ch, **bf)
         self.v = torch.empty(cfg.image, 128, dtype=torch.float32, device=dev)
         self.params = {k: torch.empty(2, 2, D, **bf) for k in ("first", "mlp", "attn", "out")}
-        self.peer = None
+        self.peer = self.peer_rs = None
         if tp and reduce_dtype == "peer":
             from . import tp as TP
             self.peer = TP.PeerReduce(tp[2], tp[0], tp[1], M, D, dev)
+        if tp and reduce_dtype == "peer_rs":
+            from . import tp as TP
+            self.peer_rs = TP.PeerRS(tp[2], tp[0], tp[1], M, D, dev)
+            self.a = self.peer_rs.a       # the gathered LayerNorm output lives where the other ranks can store it
 
     # --- per-step adaLN parameters (forward.py:231-238), computed on the GPU ---
     def set_t(self, sigma):
@@ -262,6 +275,14 @@ class DiT:
     def _branch_ln(self, x, w, xin, params, xo):
         """The out / down projection followed by the residual + LayerNorm; under tensor parallelism the partial
         projections are summed across the group first (in the LayerNorm kernel itself for reduce_dtype "peer")."""
+        if self.peer_rs is not None:    # "peer_rs": the same three steps over peer memory, no collective kernel
+            s = torch.cuda.current_stream().cuda_stream
+            slot, epoch = self.peer_rs.next()
+            self.peer_rs.gemm(x, w, slot, s)
+            self.peer_rs.signal(slot, epoch, s)
+            split = min(max(self.cfg.text - self.r0, 0), self.rows)
+            self.peer_rs.ln_mod(xin, slot, epoch, params, split, xo, s)
+            return
         if self.a_sh is not None:       # "rs": reduce-scatter, LayerNorm of this rank's rows, all-gather
             import torch.distributed as dist
             self._linear(x, w, self.c)
@@ -281,13 +302,18 @@ class DiT:
         self.peer.ln_mod(xin, slot, epoch, params, self.cfg.text, xo, self.a, s)
 
     def close(self):
-        """Release the peer buffers of reduce_dtype "peer" (a collective: every rank of the group calls it)."""
-        if self.peer is not None:
+        """Release the peer buffers of reduce_dtype "peer" / "peer_rs" (a collective: every rank of the group calls
+        it)."""
+        if self.peer is not None or self.peer_rs is not None:
             import torch.distributed as dist
             torch.cuda.synchronize(self.dev)
             dist.barrier(group=self.tp[2])
-            self.peer.close()
-            self.peer = None
+            if self.peer_rs is not None:
+                self.a = None
+            for pr in (self.peer, self.peer_rs):
+                if pr is not None:
+                    pr.close()
+            self.peer = self.peer_rs = None
 
     def _branch(self, x, w):
         """The out / down projection: bf16 on one GPU; partial sums all-reduced across the TP group."""

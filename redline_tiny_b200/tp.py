@@ -97,3 +97,108 @@ class PeerReduce:
         if self.base:
             L.call("rl_ipc_free", self.base)
             self.base = 0
+
+
+class _DeviceArray:
+    """A uint16 (rows, cols) view of memory this module owns (an IPC allocation), through the CUDA array interface
+    (no copy)."""
+
+    def __init__(self, ptr, rows, cols):
+        self.__cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<u2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerRS:
+    """Reduce-scatter + row-sharded LayerNorm + all-gather over peer memory for W ranks (reduce_dtype "peer_rs").
+
+    Rank r owns rows [r R, r R + R) of the residual stream (R = M / W, R % 16 == 0). Per sublayer:
+    the projection GEMM (rl_linear_bfp16_scatter) stores each 16-row chunk of its bf16 partial, as one 1 KB bulk copy,
+    straight into the owning rank's receive buffer (slot s, source r) - every value crosses NVLink once, to its owner,
+    while the GEMM computes; rl_tp_signal stores the epoch into every rank's pad [s][r]; rl_ln_mod_tp_rs waits for
+    the other ranks' epochs, adds the W partials of its R rows in rank order, applies the residual + LayerNorm and
+    stores its rows of y into every rank's copy of the next GEMM's A operand (`a`); rl_tp_signal on slot 2 announces
+    them and rl_tp_wait holds the stream until every rank's rows have arrived. Only 1 / W of the LayerNorm runs on a
+    rank, and no collective kernel runs.
+
+    Buffer layout (per rank, one allocation): [receive: 2 slots x W sources x R rows x D bf16 (chunk layout) | a: M x
+    D bf16 | pads: 3 slots x W uint64]. Ordering: a rank writes into another rank's receive slot s or its `a` only
+    after a wait that the other rank's later signal satisfied, and that rank signals only after the kernels that read
+    those buffers (stream order), so no write overtakes a read. Epochs are kernel arguments: eager launches only."""
+
+    def __init__(self, group, rank, world, M, D, device):
+        import torch.distributed as dist
+        if M % world or (M // world) % 16:
+            raise ValueError(f"peer_rs needs M / world to be a multiple of 16 (M={M}, world={world})")
+        self.rank, self.world, self.M, self.D = rank, world, M, D
+        self.R = M // world
+        self.r0 = rank * self.R
+        self.recv_bytes = (self.R * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.a_off = 2 * world * self.recv_bytes
+        self.pad_off = self.a_off + (M * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+        total = self.pad_off + (3 * world * 8 + _ALIGN - 1) // _ALIGN * _ALIGN
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        L.call("rl_ipc_alloc", total, ctypes.byref(ptr), handle)
+        self.base = ptr.value
+        self.opened = []
+        try:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            bases = []
+            for w, h in enumerate(handles):
+                if w == rank:
+                    bases.append(self.base)
+                    continue
+                p = ctypes.c_void_p()
+                L.call("rl_ipc_open", (ctypes.c_char * 64).from_buffer_copy(h), ctypes.byref(p))
+                self.opened.append(p.value)
+                bases.append(p.value)
+        except Exception:
+            self.close()
+            raise
+        i64 = dict(dtype=torch.int64, device=device)
+
+        def recv(b, s, src):
+            return b + (s * world + src) * self.recv_bytes
+
+        # slot s: where this rank's partial rows for owner o go, and this rank's W received partials
+        self.dsts = [torch.tensor([recv(bases[o], s, rank) for o in range(world)], **i64) for s in range(2)]
+        self.parts = [torch.tensor([recv(self.base, s, w) for w in range(world)], **i64) for s in range(2)]
+        self.y_dsts = torch.tensor([b + self.a_off + self.r0 * D * 2 for b in bases], **i64)
+        self.pads = torch.tensor([b + self.pad_off for b in bases], **i64)
+        self.a = torch.as_tensor(_DeviceArray(self.base + self.a_off, M, D), device=device).view(torch.bfloat16)
+        self.epoch = 0
+        self.group = group
+        dist.barrier(group=group)       # every rank's pads are zero and mapped before the first signal
+
+    def next(self):
+        """The (slot, epoch) of the next reduction."""
+        self.epoch += 1
+        return self.epoch & 1, self.epoch
+
+    def gemm(self, x, w, slot, stream):
+        """The projection x @ w (x: M rows), its partial rows sent to their owners' receive slot `slot`."""
+        M, K = x.shape
+        L.call("rl_linear_bfp16_scatter", x.data_ptr(), M, K, w.native.data_ptr(), w.N, self.dsts[slot].data_ptr(),
+               self.world, self.R, stream)
+
+    def signal(self, slot, epoch, stream):
+        L.call("rl_tp_signal", self.pads.data_ptr(), self.world, self.rank, slot, epoch, stream)
+
+    def ln_mod(self, x, slot, epoch, params, row_split, x_out, stream):
+        """Rows of this rank: x_out = x + g * bf16(sum of the W partials); LN(x_out) * scale into every rank's `a`,
+        then the all-gather's signal and wait."""
+        pad = self.base + self.pad_off + slot * self.world * 8
+        L.call("rl_ln_mod_tp_rs", x.data_ptr(), self.parts[slot].data_ptr(), self.world, pad, self.rank, epoch,
+               params.data_ptr(), self.R, self.D, row_split, x_out.data_ptr(), self.y_dsts.data_ptr(), stream)
+        self.signal(2, epoch, stream)
+        L.call("rl_tp_wait", self.base + self.pad_off + 2 * self.world * 8, self.world, self.rank, epoch, stream)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's; call after a barrier that follows the last use."""
+        self.a = None
+        for p in self.opened:
+            L.call("rl_ipc_close", p)
+        self.opened = []
+        if self.base:
+            L.call("rl_ipc_free", self.base)
+            self.base = 0

@@ -1,7 +1,8 @@
 """Tensor-parallel DiT on 2 GPUs (one process per GPU; the partial projections summed by the LayerNorm kernel over
-peer memory, by an NCCL reduce-scatter with the LayerNorm on each rank's rows and an all-gather of its output, or by
+peer memory, by the same reduce-scatter + row-sharded LayerNorm + all-gather over peer memory or through NCCL, or by
 an NCCL all-reduce in bf16 or fp32) against the unsharded CPU oracle: velocity cosine >= 0.999;
-the peer sum and NCCL's bf16 all-reduce agree bit for bit at 2 ranks. Needs two GPUs; skipped otherwise.
+the peer forms and NCCL's bf16 all-reduce / reduce-scatter agree bit for bit at 2 ranks. Needs two GPUs; skipped
+otherwise.
 
 The bounded wait of the fused kernel is checked on one GPU: a signal pad that no rank writes makes the wait run out,
 the kernel records the error and returns, and the context stays usable."""
@@ -36,9 +37,10 @@ def _worker(rank, world, port, q, blocks_cfg, reduce_dtype):
         v = model.forward(torch.from_numpy(lat), torch.from_numpy(txt), 0.5).float().cpu().numpy()
         ops.device_status()
         model.close()
-        if reduce_dtype == "peer":     # the same step through NCCL's bf16 all-reduce: identical at two ranks
+        twin = {"peer": "bf16", "peer_rs": "rs"}.get(reduce_dtype)
+        if twin:     # the same step through NCCL (all-reduce / reduce-scatter, bf16): identical at two ranks
             nccl = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, world), device=f"cuda:{rank}",
-                           tp=(rank, world, dist.group.WORLD), reduce_dtype="bf16")
+                           tp=(rank, world, dist.group.WORLD), reduce_dtype=twin)
             v2 = nccl.forward(torch.from_numpy(lat), torch.from_numpy(txt), 0.5).float().cpu().numpy()
             if rank == 0:
                 q.put(bool(np.array_equal(v, v2)))
@@ -55,7 +57,7 @@ def _worker(rank, world, port, q, blocks_cfg, reduce_dtype):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("reduce_dtype", ["peer", "rs", "bf16", "fp32"])
+@pytest.mark.parametrize("reduce_dtype", ["peer", "peer_rs", "rs", "bf16", "fp32"])
 @pytest.mark.parametrize("blocks_cfg", [dict(hidden=256, heads=2, ffn=512, blocks=2, text=64, image=192, grid=(12, 16)),
                                         dict(blocks=1)])
 def test_tp2_dit_matches_oracle(blocks_cfg, reduce_dtype):
@@ -72,11 +74,11 @@ def test_tp2_dit_matches_oracle(blocks_cfg, reduce_dtype):
     for p in procs:
         p.join(timeout=600)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    got = [q.get(timeout=10) for _ in range(2 if reduce_dtype == "peer" else 1)]
+    got = [q.get(timeout=10) for _ in range(2 if reduce_dtype in ("peer", "peer_rs") else 1)]
     cos = next(g for g in got if not isinstance(g, bool))
     assert cos >= 0.999, f"TP-2 velocity cosine {cos:.6f}"
-    if reduce_dtype == "peer":
-        assert next(g for g in got if isinstance(g, bool)), "peer sum differs from NCCL's bf16 all-reduce"
+    if reduce_dtype in ("peer", "peer_rs"):
+        assert next(g for g in got if isinstance(g, bool)), "peer sum differs from NCCL's bf16 reduction"
 
 
 def test_ln_mod_tp_wait_runs_out_cleanly():
@@ -110,3 +112,73 @@ def test_ln_mod_tp_wait_runs_out_cleanly():
     br = (part.float() * 2).to(torch.bfloat16).float()
     ref = (x.float() + br).to(torch.bfloat16).float()
     assert torch.equal(xo.float(), ref)
+
+
+def test_tp_wait_runs_out_cleanly():
+    """rl_tp_wait on a pad that nothing writes: the wait runs out (about two seconds), the error is reported and the
+    next launch runs; with the epochs present it passes."""
+    import torch
+    from redline_tiny_b200 import _lib as L
+    from redline_tiny_b200 import ops
+    dev = torch.device("cuda", 0)
+    pad = torch.zeros(4, dtype=torch.int64, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    L.call("rl_tp_wait", pad.data_ptr(), 4, 1, 3, s)
+    with pytest.raises(L.RedlineError):
+        ops.device_status()
+    pad.fill_(3)
+    L.call("rl_tp_wait", pad.data_ptr(), 4, 1, 3, s)
+    ops.device_status()
+
+
+def _chunked(t):
+    """(M, D) -> the partial chunk layout: 16-row x 32-column chunks of 512 values, chunk-row-major."""
+    M, D = t.shape
+    return t.view(M // 16, 16, D // 32, 32).permute(0, 2, 1, 3).contiguous()
+
+
+def test_scatter_gemm_and_rs_layernorm_one_gpu():
+    """The peer reduce-scatter pieces on one GPU with W = 2 (both ranks' buffers local): rl_linear_bfp16_scatter
+    stores rows [0, R) and [R, 2R) in the chunk layout of each block, bit-equal to rl_linear_bfp16_partial's; and
+    rl_ln_mod_tp_rs over one block equals rl_ln_mod_tp on the same rows, bit for bit, in every y destination."""
+    import torch
+    from redline_tiny_b200 import _lib as L
+    from redline_tiny_b200 import ops
+    dev = torch.device("cuda", 0)
+    s = torch.cuda.current_stream().cuda_stream
+    M, K, N, W = 512, 256, 384, 2
+    R = M // W
+    g = torch.Generator(device=dev).manual_seed(3)
+    _, x = ops.quantize_bfp16(torch.randn(M, K, generator=g, device=dev), want_bytes=False)
+    w = ops.PackedWeight.from_float(torch.randn(K, N, generator=g, device=dev) * 0.05)
+    full = torch.empty(M * N, dtype=torch.bfloat16, device=dev)
+    L.call("rl_linear_bfp16_partial", x.data_ptr(), M, K, w.native.data_ptr(), N, full.data_ptr(), None, s)
+    blocks = [torch.full((R * N,), 5.0, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    dsts = torch.tensor([b.data_ptr() for b in blocks], dtype=torch.int64, device=dev)
+    L.call("rl_linear_bfp16_scatter", x.data_ptr(), M, K, w.native.data_ptr(), N, dsts.data_ptr(), W, R, s)
+    ops.device_status()
+    for o in range(W):      # block o of the full partial is its rows' chunks: a contiguous range of chunk rows
+        assert torch.equal(blocks[o].view(torch.int16), full[o * R * N:(o + 1) * R * N].view(torch.int16))
+    # the LayerNorm of rank 1's rows from two partials
+    D = N
+    xin = torch.randn(R, D, generator=g, device=dev).to(torch.bfloat16)
+    p0 = torch.randn(R, D, generator=g, device=dev).to(torch.bfloat16)
+    p1 = torch.randn(R, D, generator=g, device=dev).to(torch.bfloat16)
+    parts = [_chunked(p0), _chunked(p1)]
+    parts_t = torch.tensor([p.data_ptr() for p in parts], dtype=torch.int64, device=dev)
+    params = (1 + 0.1 * torch.randn(2, 2, D, generator=g, device=dev)).to(torch.bfloat16)
+    pad = torch.tensor([4, 0], dtype=torch.int64, device=dev)       # rank 1 waits for rank 0's epoch 4
+    xo_ref = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    y_ref = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    L.call("rl_ln_mod_tp", xin.data_ptr(), parts_t.data_ptr(), 2, pad.data_ptr(), 1, 4, params.data_ptr(), R, D, 40,
+           xo_ref.data_ptr(), y_ref.data_ptr(), None, s)
+    xo = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    outs = [torch.zeros(M, D, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    y_dsts = torch.tensor([o[R:].data_ptr() for o in outs], dtype=torch.int64, device=dev)
+    L.call("rl_ln_mod_tp_rs", xin.data_ptr(), parts_t.data_ptr(), 2, pad.data_ptr(), 1, 4, params.data_ptr(), R, D,
+           40, xo.data_ptr(), y_dsts.data_ptr(), s)
+    ops.device_status()
+    assert torch.equal(xo.view(torch.int16), xo_ref.view(torch.int16))
+    for o in outs:
+        assert torch.equal(o[R:].view(torch.int16), y_ref.view(torch.int16))
+        assert not o[:R].float().any(), "rows of the other rank were written"
