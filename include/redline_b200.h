@@ -227,8 +227,8 @@ int rl_qkv_post_gqa(const uint16_t* qkv, const float* rope_cs, const float* w_q,
 /*
  * The QKV projection with rl_qkv_post_gqa in its epilogue: one GEMM launch in place of rl_linear_bfp16 + rl_qkv_post
  * (forward.py:245-246, the qkv_bfp artifact followed by kernels/glue/qkv_post.cc:112-178; redline/vlm_run.py:407-412
- * for grouped-query heads). x: (M, K) bf16; w_native: the packed (K, (H + 2 Hkv) * 128) QKV weight (H + 2 Hkv even,
- * K % 64 == 0). The accumulator of each head is rounded to bf16 (the projection's output dtype) and then normalised,
+ * for grouped-query heads). x: (M, K) bf16; w_native: the packed (K, (H + 2 Hkv) * 128) QKV weight (K % 64 == 0;
+ * an even head count runs on the 2-SM pair kernel, an odd one on the 1-SM kernel). The accumulator of each head is rounded to bf16 (the projection's output dtype) and then normalised,
  * rotated and stored as rl_qkv_post_gqa stores it: q (H, M, 128), k (Hkv, M, 128), vt (Hkv, 128, ldv) with columns
  * M..ldv-1 zeroed. ldv % 16 == 0 and M <= ldv <= M rounded up to a multiple of 256. Never splits K.
  */

@@ -463,7 +463,8 @@ __device__ __forceinline__ void store_a_sw128(uint8_t* a_tile, int row, int part
   fence_proxy_async_smem();
 }
 
-template <int V, int S, int G, int P>
+// E = 1: the QKV epilogue (QK-RMSNorm + RoPE, V transposed; Params::qkv_H) instead of the plain / SwiGLU stores.
+template <int V, int S, int G, int P, int E = 0>
 __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bfp16_linear_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
   using C = Cfg<V, S, G, P>;
@@ -629,6 +630,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     constexpr int NC = BN / 2 / kChunk;            // 8 chunks of 16 columns per warp
     int it = 0;
     bool ok = true;
+    [[maybe_unused]] uint32_t rms_uses = 0;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int xt = tile % p.num_x_tiles, wt = tile / p.num_x_tiles;
       const int b = (C::kAccBufs == 2) ? (it & 1) : 0;
@@ -644,6 +646,18 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + b * 256 + h * (BN / 2) + ((32u * q) << 16);
       const int64_t xb = static_cast<int64_t>(xt) * BN + h * (BN / 2);
+      if constexpr (E == 1) {
+        static_assert(C::kAccBufs == 1, "the QKV epilogue's sums are double-buffered for one accumulator");
+        if (!qkv_half(p, tbase, epi_stage, ew, lane, q, h, wt, xb, bars->rms, rms_uses, abort, [&] {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars->acce[b]);
+            })) {
+          ok = false;
+          break;
+        }
+        continue;
+      }
       // chunk by chunk: the tcgen05.ld of chunk c+1 is in flight while chunk c is converted and stored
       uint32_t ra[kChunk], rb[kChunk];
       RL_TMEM_LD16(tbase, ra);
@@ -1006,7 +1020,7 @@ inline int make_a_map(CUtensorMap* map, const uint16_t* x, const Params& p, int 
   return RL_OK;
 }
 
-template <int V, int S, int G, int P>
+template <int V, int S, int G, int P, int E = 0>
 int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
   using C = Cfg<V, S, G, P>;
   CUtensorMap tmap;
@@ -1016,12 +1030,12 @@ int launch(const uint16_t* x, const Params& p, cudaStream_t stream) {
   int dev = 0;
   RL_TRY_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    RL_TRY_CUDA(cudaFuncSetAttribute(bfp16_linear_kernel<V, S, G, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    RL_TRY_CUDA(cudaFuncSetAttribute(bfp16_linear_kernel<V, S, G, P, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::kSmemBytes));
     attr_set[dev] = true;
   }
   const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-  bfp16_linear_kernel<V, S, G, P><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tmap, p);
+  bfp16_linear_kernel<V, S, G, P, E><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tmap, p);
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }
@@ -1297,8 +1311,8 @@ int rl_qkv_linear(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_nati
   using namespace rl;
   using namespace rl::gemm;
   RL_REQUIRE(x && w_native && rope_cs && w_q && w_k && q && k && vt, RL_ERR_ARGUMENT, "rl_qkv_linear: NULL pointer");
-  RL_REQUIRE(H > 0 && Hkv > 0 && H % Hkv == 0 && (H + 2 * Hkv) % 2 == 0 && M >= 0 && K >= 64 && K % 64 == 0,
-             RL_ERR_ARGUMENT, "rl_qkv_linear: need H, Hkv > 0, H %% Hkv == 0, H + 2 Hkv even, K %% 64 == 0");
+  RL_REQUIRE(H > 0 && Hkv > 0 && H % Hkv == 0 && M >= 0 && K >= 64 && K % 64 == 0, RL_ERR_ARGUMENT,
+             "rl_qkv_linear: need H, Hkv > 0, H %% Hkv == 0, K %% 64 == 0");
   RL_REQUIRE(ldv >= M && ldv % 16 == 0 && ldv <= (M + BN - 1) / BN * BN, RL_ERR_ARGUMENT,
              "rl_qkv_linear: need M <= ldv <= M rounded up to 256, ldv %% 16 == 0 (M=%lld ldv=%lld)", (long long)M,
              (long long)ldv);
@@ -1334,7 +1348,9 @@ int rl_qkv_linear(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_nati
   p.k_out = k;
   p.vt_out = vt;
   p.ldv = ldv;
-  return launch_pair<kTmemA, 8, 2, 2, 1>(x, p, stream);
+  // whole 256-column head pairs on the 2-SM pair kernel, else (an odd head count) the 1-SM kernel
+  if (p.num_w_tiles % 2 == 0) return launch_pair<kTmemA, 8, 2, 2, 1>(x, p, stream);
+  return launch<kTmemA, 4, 2, 2, 1>(x, p, stream);
 }
 
 int rl_linear_bfp16_partial(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,

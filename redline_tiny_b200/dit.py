@@ -124,8 +124,8 @@ class DiT:
     (default: "peer" at 2 GPUs, where the transfer overlaps the GEMM; "bf16" above - at 4 GPUs NCCL's all-reduce of
     26.7 MB took ~97 us against ~73 us each for its reduce-scatter and all-gather, which outweighs the LayerNorm work
     "rs" saves: 22.7 against 23.9 ms per step).
-    fuse_qkv: QK-RMSNorm + RoPE run in the QKV GEMM's epilogue (rl_qkv_linear, when the local head count is even)
-    instead of rl_qkv_post after the GEMM."""
+    fuse_qkv: QK-RMSNorm + RoPE run in the QKV GEMM's epilogue (rl_qkv_linear) instead of rl_qkv_post after the
+    GEMM."""
 
     def __init__(self, cfg, weights, device="cuda", tp=None, reduce_dtype="auto", fuse_qkv=True):
         if reduce_dtype not in ("auto", "peer", "peer_rs", "rs", "bf16", "fp32"):
@@ -333,7 +333,7 @@ class DiT:
         cfg, b = self.cfg, self.blocks[i]
         s = torch.cuda.current_stream().cuda_stream
         M, H = cfg.M, self.heads_local
-        if self.fuse_qkv and H % 2 == 0:   # QK-RMSNorm + RoPE in the QKV GEMM's epilogue (pairs of heads per tile)
+        if self.fuse_qkv:   # QK-RMSNorm + RoPE in the QKV GEMM's epilogue
             L.call("rl_qkv_linear", self.a.data_ptr(), M, self.a.shape[1], b["qkv"].native.data_ptr(), H, H,
                    self.rope_cs.data_ptr(), b["wq"].data_ptr(), b["wk"].data_ptr(), self.q.data_ptr(),
                    self.k.data_ptr(), self.vt.data_ptr(), self.ldv, s)

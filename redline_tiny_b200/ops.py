@@ -224,7 +224,7 @@ def qkv_post(qkv, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
 
 def qkv_linear(x_dq, w, rope_cs, w_q, w_k, heads, ldv=None, kv_heads=None):
     """linear_bfp16(x_dq, w) followed by qkv_post in one GEMM launch (the norm and RoPE run in the GEMM's epilogue):
-    w = the packed (K, (H + 2 Hkv) * 128) QKV weight with H + 2 Hkv even. Outputs as qkv_post."""
+    w = the packed (K, (H + 2 Hkv) * 128) QKV weight. Outputs as qkv_post."""
     _check_cuda(x_dq, w.native, rope_cs, w_q, w_k)
     M, K = x_dq.shape
     hkv = heads if kv_heads is None else int(kv_heads)

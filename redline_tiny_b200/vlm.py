@@ -91,7 +91,7 @@ class LM:
         self.a = torch.empty(M, D, **bf)
         self.qkv = torch.empty(M, (H + 2 * Hk) * HEAD_DIM, **bf)
         self.ldv = (M + 127) // 128 * 128
-        self.fuse_qkv = fuse_qkv and (cfg.heads + 2 * cfg.kv_heads) % 2 == 0   # rl_qkv_linear: whole head pairs
+        self.fuse_qkv = fuse_qkv   # QK-RMSNorm + RoPE in the QKV GEMM's epilogue (rl_qkv_linear)
         self.q = torch.empty(H, M, HEAD_DIM, **bf)
         self.k = torch.empty(Hk, M, HEAD_DIM, **bf)
         self.vt = torch.zeros(Hk, HEAD_DIM, self.ldv, **bf)

@@ -154,10 +154,12 @@ def test_qkv_post(env, golden, M, H):
 
 
 @pytest.mark.parametrize("M,K,H,Hkv,ldv", [(300, 256, 2, 2, None), (300, 512, 4, 1, 304), (200, 512, 4, 1, 256),
-                                           (1088, 2048, 32, 8, None), (4352, 3072, 24, 24, None)])
+                                           (1088, 2048, 32, 8, None), (4352, 3072, 24, 24, None),
+                                           (300, 256, 1, 1, None), (4352, 3072, 3, 3, None)])
 def test_qkv_linear_fused(env, M, K, H, Hkv, ldv):
     """rl_qkv_linear (QK-RMSNorm + RoPE in the QKV GEMM's epilogue) against the two-launch form it replaces:
-    rl_linear_bfp16 (the same pair kernel, so the same fp32 accumulators) followed by rl_qkv_post_gqa. V is the same
+    rl_linear_bfp16 (the same kernel - the 2-SM pair kernel for an even head count, the 1-SM one for an odd count -
+    so the same fp32 accumulators) followed by rl_qkv_post_gqa. V is the same
     bf16 rounding of the same accumulator: bit-exact, zero columns M..ldv-1 included. q / k sum their squares in
     another order and may contract the RoPE products into FMAs differently, so a value may land one bf16 step away:
     >= 97% bit-identical, and within 2^-6 of the head's largest |value|; both forms meet the oracle's rms_rope bar
@@ -211,9 +213,9 @@ def test_qkv_linear_rejects_bad_shapes(env):
     x = torch.zeros(64, 128, dtype=torch.bfloat16, device=dev)
     cs = torch.zeros(64, 64, 2, device=dev)
     wn = torch.ones(128, device=dev)
-    w3 = ops.PackedWeight.from_float(torch.zeros(128, 3 * 128, device=dev))   # 3 heads: not whole head pairs
+    w3 = ops.PackedWeight.from_float(torch.zeros(128, 3 * 128, device=dev))
     with pytest.raises(L.RedlineError):
-        ops.qkv_linear(x, w3, cs, wn, wn, 1)
+        ops.qkv_linear(torch.zeros(64, 96, dtype=torch.bfloat16, device=dev), w3, cs, wn, wn, 1)   # K % 64 != 0
     w4 = ops.PackedWeight.from_float(torch.zeros(128, 4 * 128, device=dev))   # H 2, Hkv 1
     with pytest.raises(ValueError):
         ops.qkv_linear(x, w4, cs, wn, wn, 2)                                  # Hkv 2 would need 6 heads
