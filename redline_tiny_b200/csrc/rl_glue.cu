@@ -188,6 +188,123 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
   }
 }
 
+// The same math with one 128-thread CTA per row, for row counts too small to fill the GPU with one warp per row (the
+// tensor-parallel row shards: 2176, 1088, 544 rows): thread t owns the blocks t, t + 128, ... (NB of them, D <=
+// 8192), issues all of the row's loads before it uses any and keeps x' in registers between the passes, and the
+// four warps add their sums once per row (in warp order: a fixed summation order). A warp-per-row pass walks the
+// row's 12 blocks per lane one load at a time; with few rows that chain of dependent loads, not bandwidth, set the
+// time (a LayerNorm of 1088 rows took as long as one of 4352).
+constexpr int kRowThreads = 128;
+constexpr int kRowMaxNB = 8;
+
+template <int NB>
+__global__ void __launch_bounds__(kRowThreads, NB <= 2 ? 8 : (NB <= 4 ? 6 : 4))
+    ln_mod_row_kernel(const uint16_t* __restrict__ x, const void* __restrict__ br, int br_f32, TpBranch tp,
+                      const unsigned long long* pad, int rank, unsigned long long epoch,
+                      const uint16_t* __restrict__ params, int64_t M, int64_t D, int64_t row_split, float eps,
+                      int rms, uint16_t* __restrict__ xo, uint16_t* __restrict__ y_dq, uint8_t* __restrict__ y_q,
+                      YPeers yp) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int64_t KB = D >> 3;
+  __shared__ float red[2][4][2];   // per-warp (sum, sum of squares), two rows apart
+  if (tp.W > 0) {
+    __shared__ int ready;
+    if (t == 0) {
+      int ok = 1;
+      for (int w = 0; ok && w < tp.W; ++w) {
+        if (w == rank) continue;
+        const long long t0 = clock64();
+        while (true) {
+          unsigned long long v;
+          asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pad + w) : "memory");
+          if (v >= epoch) break;
+          if (clock64() - t0 > RL_WAIT_LIMIT_CYCLES) {
+            report(kErrWaitTimeout);
+            ok = 0;
+            break;
+          }
+          __nanosleep(200);
+        }
+      }
+      ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
+    br_f32 = 1;
+  }
+  int it = 0;
+  for (int64_t r = blockIdx.x; r < M; r += gridDim.x, ++it) {
+    const uint16_t* prow = params + (r < row_split ? 2 * D : 0);
+    uint4 xr[NB], gr[NB];
+    float v[NB][8];
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int64_t kb = t + kRowThreads * i;
+      if (kb < KB) {
+        xr[i] = __ldg(reinterpret_cast<const uint4*>(x + r * D) + kb);
+        gr[i] = __ldg(reinterpret_cast<const uint4*>(prow) + kb);
+        load_branch(br, br_f32, tp, r, D, kb, v[i]);
+      }
+    }
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int64_t kb = t + kRowThreads * i;
+      if (kb < KB) {
+        float xf[8], gf[8];
+        unpack8(xr[i], xf);
+        unpack8(gr[i], gf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float b = br_f32 ? bf16_bits_to_float(float_to_bf16_bits(v[i][j])) : v[i][j];
+          v[i][j] = bf16_bits_to_float(float_to_bf16_bits(__fadd_rn(xf[j], __fmul_rn(gf[j], b))));
+          s1 += v[i][j];
+          s2 = fmaf(v[i][j], v[i][j], s2);
+        }
+        if (xo) reinterpret_cast<uint4*>(xo + r * D)[kb] = pack8(v[i]);
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
+      red[it & 1][warp][0] = s1;
+      red[it & 1][warp][1] = s2;
+    }
+    __syncthreads();   // a buffer is written again two rows later, after every thread passed the next row's barrier
+    s1 = red[it & 1][0][0] + red[it & 1][1][0] + red[it & 1][2][0] + red[it & 1][3][0];
+    s2 = red[it & 1][0][1] + red[it & 1][1][1] + red[it & 1][2][1] + red[it & 1][3][1];
+    const float mean = rms ? 0.0f : s1 / static_cast<float>(D);
+    const float var = rms ? s2 / static_cast<float>(D) : fmaxf(s2 / static_cast<float>(D) - mean * mean, 0.0f);
+    const float rstd = 1.0f / sqrtf(var + eps);
+    const uint16_t* sc = prow + D;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int64_t kb = t + kRowThreads * i;
+      if (kb < KB) {
+        float sf[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(sc) + kb), sf);
+        uint32_t bits[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bits[j] = __float_as_uint((v[i][j] - mean) * rstd * sf[j]);
+        uint32_t E, lo, hi, wq[4];
+        bfp16_quant_block_fast(bits, E, lo, hi, wq);
+        const uint4 yv = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+        if (y_dq) reinterpret_cast<uint4*>(y_dq + r * D)[kb] = yv;
+        for (int k = 0; k < yp.n; ++k) reinterpret_cast<uint4*>(yp.dst[k] + r * D)[kb] = yv;
+        if (y_q) {
+          uint8_t* dst = y_q + (r * KB + kb) * 9;
+          dst[0] = static_cast<uint8_t>(E);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[1 + j] = static_cast<uint8_t>(lo >> (8 * j));
+            dst[5 + j] = static_cast<uint8_t>(hi >> (8 * j));
+          }
+        }
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
@@ -293,13 +410,30 @@ inline int grid_rows(int64_t units, int per_cta) {
   return static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
 }
 
-// Residual + LayerNorm / RMSNorm launch (rl_ln_mod, rl_rms_mod, rl_ln_mod_tp).
+// Residual + LayerNorm / RMSNorm launch (rl_ln_mod, rl_rms_mod, rl_ln_mod_tp, rl_ln_mod_tp_rs): one warp per row
+// when there are rows for at least two warps per SM-slot of the grid (4352 rows of config 4), else one CTA per row
+// (D <= 8192).
 inline int launch_ln_mod(const uint16_t* x, const void* br, int br_f32, TpBranch tp, const unsigned long long* pad,
                          int rank, unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D,
                          int64_t row_split, float eps, int rms, uint16_t* xo, uint16_t* y_dq, uint8_t* y_q,
                          cudaStream_t stream, YPeers yp = YPeers{nullptr, 0}) {
-  ln_mod_kernel<<<grid_rows(M, kWarps), kThreads, 0, stream>>>(x, br, br_f32, tp, pad, rank, epoch, params, M, D,
-                                                               row_split, eps, rms, xo, y_dq, y_q, yp);
+  const int nb = static_cast<int>(((D >> 3) + kRowThreads - 1) / kRowThreads);
+  if (nb > kRowMaxNB || M > static_cast<int64_t>(sm_count()) * 2 * kWarps) {
+    ln_mod_kernel<<<grid_rows(M, kWarps), kThreads, 0, stream>>>(x, br, br_f32, tp, pad, rank, epoch, params, M, D,
+                                                                 row_split, eps, rms, xo, y_dq, y_q, yp);
+  } else {
+    const unsigned grid = static_cast<unsigned>(M);
+#define RL_LN_ROW(N)                                                                                                \
+  case N:                                                                                                           \
+    ln_mod_row_kernel<N><<<grid, kRowThreads, 0, stream>>>(x, br, br_f32, tp, pad, rank, epoch, params, M, D,      \
+                                                           row_split, eps, rms, xo, y_dq, y_q, yp);                 \
+    break;
+    switch (nb) {
+      RL_LN_ROW(1) RL_LN_ROW(2) RL_LN_ROW(3) RL_LN_ROW(4) RL_LN_ROW(5) RL_LN_ROW(6) RL_LN_ROW(7) RL_LN_ROW(8)
+      default: break;
+    }
+#undef RL_LN_ROW
+  }
   RL_TRY_CUDA(cudaGetLastError());
   return RL_OK;
 }

@@ -81,6 +81,29 @@ def test_tp2_dit_matches_oracle(blocks_cfg, reduce_dtype):
         assert next(g for g in got if isinstance(g, bool)), "peer sum differs from NCCL's bf16 reduction"
 
 
+@pytest.mark.parametrize("reduce_dtype", ["peer_rs", "rs", "bf16"])
+def test_tp4_dit_matches_oracle(reduce_dtype):
+    """The reductions that run on more than 2 GPUs, at 4 ranks (a 4-head, 2-block toy whose 256 rows shard into
+    blocks of 64): velocity cosine >= 0.999 against the unsharded CPU oracle. Needs four GPUs; skipped otherwise."""
+    import torch
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = next(_PORTS)
+    cfg = dict(hidden=512, heads=4, ffn=1024, blocks=2, text=64, image=192, grid=(12, 16))
+    procs = [ctx.Process(target=_worker, args=(r, 4, port, q, cfg, reduce_dtype)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = [q.get(timeout=10) for _ in range(2 if reduce_dtype == "peer_rs" else 1)]
+    cos = next(g for g in got if not isinstance(g, bool))
+    assert cos >= 0.999, f"TP-4 velocity cosine {cos:.6f}"
+
+
 def test_ln_mod_tp_wait_runs_out_cleanly():
     """rl_ln_mod_tp with W = 2 and a pad the other rank never writes: after its bounded wait (about two seconds) the
     kernel records the timeout and returns without writing; rl_device_status reports it, and the next launch runs."""
