@@ -573,9 +573,10 @@ def measure_configs(dev, stream, ws, rank):
     if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1
         import torch.distributed as dist
         # the default reduction (at 2 GPUs the projection GEMM stores its bf16 partial into the other rank's memory
-        # and the LayerNorm kernel adds both; above 2 an NCCL all-reduce of the bf16 partials), the NCCL
-        # reduce-scatter + row-sharded LayerNorm + all-gather, or at 2 GPUs the NCCL all-reduce, beside it, and the
-        # NCCL all-reduce of fp32 partials. Parity:
+        # and the LayerNorm kernel adds both; above 2 the same GEMM stores each row block into its owner's memory,
+        # the owner's LayerNorm adds them and stores its rows into every rank's next A operand), and beside it the
+        # other forms: at 2 GPUs the peer reduce-scatter form and NCCL's bf16 all-reduce, above 2 NCCL's bf16
+        # all-reduce and its reduce-scatter + all-gather; and NCCL's all-reduce of fp32 partials. Parity:
         # the TP velocity against the unsharded model's on the same weights and inputs. Partials rounded to bf16
         # before they are added move every branch value by up to half a bf16 step, and the unsharded model itself
         # moves as far when its text input moves by half a bf16 step (velocity_cos_under_half_ulp_input_change), so
@@ -588,7 +589,8 @@ def measure_configs(dev, stream, ws, rank):
                  "rs": "NCCL reduce-scatter + LayerNorm on M/N rows + NCCL all-gather",
                  "bf16": "NCCL all-reduce, bf16 (LayerNorm replicated)",
                  "fp32": "NCCL all-reduce, fp32 partials (LayerNorm replicated)"}
-        for mode in ("auto", "peer_rs", "bf16" if ws == 2 else "rs", "fp32"):
+        # "auto" is "peer" at 2 GPUs and "peer_rs" above; the other forms are timed and checked beside it
+        for mode in (("auto", "peer_rs", "bf16", "fp32") if ws == 2 else ("auto", "bf16", "rs", "fp32")):
             w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
             tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD),
                                reduce_dtype=mode)

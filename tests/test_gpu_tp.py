@@ -14,7 +14,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-_PORTS = iter(range(29800 + (os.getpid() % 40) * 10, 29800 + (os.getpid() % 40) * 10 + 10))
+_PORTS = iter(range(29800 + (os.getpid() % 40) * 40, 29800 + (os.getpid() % 40) * 40 + 40))
 
 
 def _worker(rank, world, port, q, blocks_cfg, reduce_dtype):
