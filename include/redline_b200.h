@@ -354,9 +354,7 @@ int rl_tp_signal(void* const* pads, int W, int rank, int slot, unsigned long lon
  * of W pointers: rank o's receive buffer for this rank's partial; peers over NVLink); every value crosses to its
  * owner once. rl_ln_mod_tp_rs: rl_ln_mod_tp over this rank's R rows (x, x_out: R x D; parts: the W received partials,
  * R-row chunk layout, summed in rank order; row_split relative to the block) that stores y into every rank's copy of
- * the next GEMM's A operand (y_dsts: device array of W pointers to row r0 = rank x R of each copy); with done_pads
- * (rl_tp_signal's pads array, or NULL) the kernel itself then posts epoch into slot done_slot of every rank's pad,
- * as rl_tp_signal would after it (counter: a zeroed device uint32 of this rank, reused by every call). rl_tp_wait: a
+ * the next GEMM's A operand (y_dsts: device array of W pointers to row r0 = rank x R of each copy). rl_tp_wait: a
  * bounded wait on the stream until every other rank's entry of pad (this rank's, W uint64) reaches epoch; it runs
  * between rl_tp_signal of the all-gather and the GEMM that reads the gathered rows. On a timeout the kernel records
  * the error for rl_device_status and returns. */
@@ -364,8 +362,7 @@ int rl_linear_bfp16_scatter(const uint16_t* x, int64_t M, int64_t K, const uint8
                             uint16_t* const* dsts, int W, int64_t rows_per_rank, rl_stream_t stream);
 int rl_ln_mod_tp_rs(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
                     unsigned long long epoch, const uint16_t* params, int64_t R, int64_t D, int64_t row_split,
-                    uint16_t* x_out, uint16_t* const* y_dsts, void* const* done_pads, int done_slot,
-                    unsigned int* counter, rl_stream_t stream);
+                    uint16_t* x_out, uint16_t* const* y_dsts, rl_stream_t stream);
 int rl_tp_wait(const unsigned long long* pad, int W, int rank, unsigned long long epoch, rl_stream_t stream);
 int rl_ln_mod_tp(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
                  unsigned long long epoch, const uint16_t* params, int64_t M, int64_t D, int64_t row_split,

@@ -63,8 +63,7 @@ SIGNATURES = {
     "rl_linear_bfp16_mirror": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _P, _I, _P]),
     "rl_linear_bfp16_partial": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _P]),
     "rl_linear_bfp16_scatter": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _I64, _P]),
-    "rl_ln_mod_tp_rs": (_I, [_P, _P, _I, _P, _I, ctypes.c_ulonglong, _P, _I64, _I64, _I64, _P, _P, _P, _I, _P,
-                             _P]),
+    "rl_ln_mod_tp_rs": (_I, [_P, _P, _I, _P, _I, ctypes.c_ulonglong, _P, _I64, _I64, _I64, _P, _P, _P]),
     "rl_tp_wait": (_I, [_P, _I, _I, ctypes.c_ulonglong, _P]),
     "rl_ipc_alloc": (_I, [_I64, _P, _P]),
     "rl_ipc_open": (_I, [_P, _P]),

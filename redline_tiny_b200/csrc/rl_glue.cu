@@ -47,34 +47,10 @@ struct TpBranch {
 };
 // Extra destinations of y (the tensor-parallel all-gather: this rank's rows of the LayerNorm output stored into every
 // rank's copy of the next GEMM's A operand, peers over NVLink): a device array of n row-0 pointers, or n = 0.
-// With `counter` set, the CTA that finishes last also posts `epoch` into entry [slot][rank] of every rank's signal
-// pad (pads: device array of n pad bases, each n x slots uint64), in place of a separate signal kernel: each CTA
-// makes its stores visible system-wide and counts itself, and the last one (which resets the counter for the next
-// launch) publishes the epoch with a system-scope release store.
 struct YPeers {
   uint16_t* const* dst;
   int n;
-  unsigned int* counter = nullptr;
-  unsigned long long* const* pads = nullptr;
-  int slot = 0, rank = 0;
-  unsigned long long epoch = 0;
 };
-
-__device__ __forceinline__ void tp_done_signal(const YPeers& yp) {
-  if (!yp.counter) return;
-  __syncthreads();               // every thread of this CTA has issued its stores
-  if (threadIdx.x == 0) {
-    __threadfence_system();      // ... and they are visible to the other GPUs before this CTA is counted
-    if (atomicAdd(yp.counter, 1u) == gridDim.x - 1) {
-      atomicExch(yp.counter, 0u);
-      __threadfence_system();
-      for (int r = 0; r < yp.n; ++r) {
-        unsigned long long* dst = yp.pads[r] + static_cast<int64_t>(yp.slot) * yp.n + yp.rank;
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(yp.epoch) : "memory");
-      }
-    }
-  }
-}
 
 __device__ __forceinline__ void load_branch(const void* br, int br_f32, TpBranch tp, int64_t r, int64_t D, int64_t kb,
                                             float (&f)[8]) {
@@ -210,7 +186,6 @@ __global__ void __launch_bounds__(kThreads) ln_mod_kernel(const uint16_t* __rest
       }
     }
   }
-  tp_done_signal(yp);
 }
 
 // The same math with one 128-thread CTA per row, for row counts too small to fill the GPU with one warp per row (the
@@ -328,7 +303,6 @@ __global__ void __launch_bounds__(kRowThreads, NB <= 2 ? 8 : (NB <= 4 ? 6 : 4))
       }
     }
   }
-  tp_done_signal(yp);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {

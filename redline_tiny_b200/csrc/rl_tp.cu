@@ -96,11 +96,10 @@ int rl_tp_wait(const unsigned long long* pad, int W, int rank, unsigned long lon
 
 int rl_ln_mod_tp_rs(const uint16_t* x, const uint16_t* const* parts, int W, const unsigned long long* pad, int rank,
                     unsigned long long epoch, const uint16_t* params, int64_t R, int64_t D, int64_t row_split,
-                    uint16_t* x_out, uint16_t* const* y_dsts, void* const* done_pads, int done_slot,
-                    unsigned int* counter, rl_stream_t stream) {
+                    uint16_t* x_out, uint16_t* const* y_dsts, rl_stream_t stream) {
   using namespace rl;
   RL_REQUIRE(x && parts && pad && params && x_out && y_dsts && W >= 1 && W <= 64 && rank >= 0 && rank < W &&
-                 epoch > 0 && (!done_pads || (counter && done_slot >= 0)),
+                 epoch > 0,
              RL_ERR_ARGUMENT, "rl_ln_mod_tp_rs: bad arguments");
   RL_REQUIRE(R >= 0 && R % 16 == 0 && D >= 8 && D % 8 == 0, RL_ERR_ARGUMENT,
              "rl_ln_mod_tp_rs: need R %% 16 == 0 and D %% 8 == 0");
@@ -108,16 +107,8 @@ int rl_ln_mod_tp_rs(const uint16_t* x, const uint16_t* const* parts, int W, cons
              RL_ERR_ALIGNMENT, "rl_ln_mod_tp_rs: bf16 pointers must be 16-byte aligned");
   RL_REQUIRE(device_is_sm100(), RL_ERR_UNSUPPORTED, "rl_ln_mod_tp_rs: needs an sm_100 device");
   if (R == 0) return RL_OK;
-  glue::YPeers yp{y_dsts, W};
-  if (done_pads) {
-    yp.counter = counter;
-    yp.pads = reinterpret_cast<unsigned long long* const*>(done_pads);
-    yp.slot = done_slot;
-    yp.rank = rank;
-    yp.epoch = epoch;
-  }
   return glue::launch_ln_mod(x, nullptr, 0, glue::TpBranch{parts, W}, pad, rank, epoch, params, R, D, row_split,
-                             1e-6f, 0, x_out, nullptr, nullptr, stream, yp);
+                             1e-6f, 0, x_out, nullptr, nullptr, stream, glue::YPeers{y_dsts, W});
 }
 
 // Peer-readable buffers: a plain cudaMalloc allocation shared through a CUDA IPC handle (64 bytes), opened by the

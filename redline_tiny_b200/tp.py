@@ -116,8 +116,8 @@ class PeerRS:
     straight into the owning rank's receive buffer (slot s, source r) - every value crosses NVLink once, to its owner,
     while the GEMM computes; rl_tp_signal stores the epoch into every rank's pad [s][r]; rl_ln_mod_tp_rs waits for
     the other ranks' epochs, adds the W partials of its R rows in rank order, applies the residual + LayerNorm and
-    stores its rows of y into every rank's copy of the next GEMM's A operand (`a`); its last CTA announces them in
-    slot 2 of every rank's pad and rl_tp_wait holds the stream until every rank's rows have arrived. Only 1 / W of the LayerNorm runs on a
+    stores its rows of y into every rank's copy of the next GEMM's A operand (`a`); rl_tp_signal on slot 2 announces
+    them and rl_tp_wait holds the stream until every rank's rows have arrived. Only 1 / W of the LayerNorm runs on a
     rank, and no collective kernel runs.
 
     Buffer layout (per rank, one allocation): [receive: 2 slots x W sources x R rows x D bf16 (chunk layout) | a: M x
@@ -165,7 +165,6 @@ class PeerRS:
         self.parts = [torch.tensor([recv(self.base, s, w) for w in range(world)], **i64) for s in range(2)]
         self.y_dsts = torch.tensor([b + self.a_off + self.r0 * D * 2 for b in bases], **i64)
         self.pads = torch.tensor([b + self.pad_off for b in bases], **i64)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=device)   # the LayerNorm's last-CTA count
         self.a = torch.as_tensor(_DeviceArray(self.base + self.a_off, M, D), device=device).view(torch.bfloat16)
         self.epoch = 0
         self.group = group
@@ -190,8 +189,8 @@ class PeerRS:
         then the all-gather's signal and wait."""
         pad = self.base + self.pad_off + slot * self.world * 8
         L.call("rl_ln_mod_tp_rs", x.data_ptr(), self.parts[slot].data_ptr(), self.world, pad, self.rank, epoch,
-               params.data_ptr(), self.R, self.D, row_split, x_out.data_ptr(), self.y_dsts.data_ptr(),
-               self.pads.data_ptr(), 2, self.counter.data_ptr(), stream)     # the kernel posts slot 2 itself
+               params.data_ptr(), self.R, self.D, row_split, x_out.data_ptr(), self.y_dsts.data_ptr(), stream)
+        self.signal(2, epoch, stream)
         L.call("rl_tp_wait", self.base + self.pad_off + 2 * self.world * 8, self.world, self.rank, epoch, stream)
 
     def close(self):
