@@ -668,9 +668,7 @@ def run_ours(args, ws, rank, local):
         sets.append((x, w_full.shard(rank, ws)[0], b[n0:n0 + ncols].contiguous(), b))
     dq = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
     out = torch.empty((M, ncols), dtype=torch.bfloat16, device=dev)
-    # K-split partials, if the shape splits: a uniform split-K when the tiles fill few clusters, or the split of the
-    # partial last wave's tiles over the clusters that would idle (C1: 816 pair tiles on 74 clusters, the last 2)
-    gws = ops.gemm_workspace(M, K, ncols, dev, epilogue=L.RL_EPI_BIAS)
+    gws = ops.gemm_workspace(M, K, ncols, dev, epilogue=L.RL_EPI_BIAS)   # split-K partials, if the shape splits
     gws_ptr, gws_bytes = (0, 0) if gws is None else (gws.data_ptr(), gws.numel())
 
     # the timed loop calls the C ABI directly on preallocated buffers (no allocation inside a step)

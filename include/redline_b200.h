@@ -136,15 +136,12 @@ int rl_weights_shard(int64_t K, int64_t N, int rank, int world, int64_t* n0, int
 int rl_linear_bfp16(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                     const uint16_t* bias, int epilogue, void* out, int out_dtype, rl_stream_t stream);
 
-/* rl_linear_bfp16 with a caller workspace for split-K (N % 256 == 0). When the pair kernel's grid would fill less
- * than the GPU (few tiles, long K), K is split into S ranges whose fp32 partials go to the workspace and one
- * HBM-bound kernel adds them (+ bias) into out (S * M * N * 4 bytes). When the tiles fill the resident clusters
- * several times over plus a few (at most half a wave), only those last tiles are split along K over the clusters
- * that would otherwise idle, their 256 x 256 fp32 partial tiles go to the workspace and a small kernel adds them
- * into out (tail tiles x splits x 256 KB). rl_linear_bfp16_workspace(M, K, N, epilogue) gives the bytes (0 when
- * no split helps, or for the SwiGLU epilogue); with a smaller workspace, a NULL one or a non-default kernel variant
- * the call is rl_linear_bfp16. The result differs from the unsplit one only by fp32 summation order, in the split
- * tiles. */
+/* rl_linear_bfp16 with a caller workspace for split-K: when the pair kernel's grid would fill less than the GPU
+ * (N % 256 == 0, few tiles, long K), K is split into S ranges whose fp32 partials go to the workspace and one
+ * HBM-bound kernel adds them (+ bias) into out. rl_linear_bfp16_workspace(M, K, N, epilogue) gives the bytes
+ * (S * M * N * 4; 0 when no split helps, or for the SwiGLU epilogue); with a smaller workspace, a NULL one or a
+ * non-default kernel variant the call is rl_linear_bfp16. The result differs from the unsplit one only by fp32
+ * summation order. */
 size_t rl_linear_bfp16_workspace(int64_t M, int64_t K, int64_t N, int epilogue);
 int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
                        const uint16_t* bias, int epilogue, void* out, int out_dtype, void* workspace,

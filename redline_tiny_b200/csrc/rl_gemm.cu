@@ -79,11 +79,6 @@ struct Params {
   int splits;            // pair kernel: K split into this many ranges, fp32 partials split_stride elements apart
   int64_t split_stride;
   int group_x = 0;       // pair kernel tile order: groups of group_x activation tiles (0: one group; pair_tile_coords)
-  // pair kernel with splits == 1: the last tail_tiles pair tiles (in tile order: the partial last wave) are split
-  // into tail_splits K ranges each, whose fp32 partial tiles (256 rows x 256 columns, dense) go to tail_ws for
-  // tail_reduce_kernel; every other tile is computed whole and stored by the normal epilogue
-  int tail_tiles = 0, tail_splits = 1;
-  float* tail_ws = nullptr;
   void* mirror = nullptr;  // bf16 output without SwiGLU: every 16-byte store of `out` is repeated here (same layout;
                            // a peer GPU's buffer for the tensor-parallel reduction)
   int chunked = 0;         // bf16 output in 16-row x 32-column chunks of 1 KB (the tensor-parallel partial layout)
@@ -749,53 +744,6 @@ __device__ __forceinline__ void pair_tile_coords(const Params& p, int tt, int np
   xt = x0 + (r - wp * gx);
 }
 
-// Work item t of the pair kernel: its pair tile tt (tile order), K steps [kt0, kt0 + kts), and slot: the uniform
-// split's index (fp32 partial at slot * split_stride), or, in the tail split, -1 for a whole tile and the partial
-// tile's index in tail_ws for a tail item.
-__device__ __forceinline__ int pair_items(const Params& p, int ntiles) {
-  return p.tail_tiles > 0 ? ntiles - p.tail_tiles + p.tail_tiles * p.tail_splits : ntiles * p.splits;
-}
-__device__ __forceinline__ void pair_item(const Params& p, int t, int ntiles, int& tt, int& kt0, int& kts, int& slot) {
-  if (p.tail_tiles > 0) {
-    const int nfull = ntiles - p.tail_tiles;
-    if (t < nfull) {
-      tt = t;
-      kt0 = 0;
-      kts = p.KT;
-      slot = -1;
-    } else {
-      const int j = t - nfull;
-      tt = nfull + j / p.tail_splits;
-      kts = p.KT / p.tail_splits;
-      kt0 = (j % p.tail_splits) * kts;
-      slot = j;
-    }
-  } else {
-    kts = p.KT / p.splits;
-    tt = t % ntiles;
-    slot = t / ntiles;
-    kt0 = slot * kts;
-  }
-}
-
-// One 16-row chunk of a tail item's fp32 partial: rows r0 .. r0 + 15 of the pair tile (rows_left of them below M),
-// this warp's 32 columns of CTA `rank`'s 128, into the dense 256 x 256 partial tile.
-__device__ __forceinline__ void tail_chunk(float* tile, const uint32_t (&r)[kChunk], uint8_t* st, int lane, int q,
-                                           int rank, int r0, int64_t rows_left) {
-  float* s32 = reinterpret_cast<float*>(st);
-#pragma unroll
-  for (int j = 0; j < kChunk; ++j) s32[j * 32 + lane] = __uint_as_float(r[j]);
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int idx = lane + 32 * i, rr = idx >> 3, part = idx & 7;
-    if (rr < rows_left)
-      *reinterpret_cast<uint4*>(tile + (r0 + rr) * 256 + rank * 128 + 32 * q + part * 4) =
-          reinterpret_cast<const uint4*>(s32 + rr * 32)[part];
-  }
-  __syncwarp();
-}
-
 // E = 1: the QKV epilogue (QK-RMSNorm + RoPE, V transposed; Params::qkv_H) instead of the plain / SwiGLU stores.
 template <int V, int S, int G, int P, int E = 0>
 __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
@@ -813,8 +761,8 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
   const int npairs = p.num_w_tiles / 2;
   const int ntiles = p.num_x_tiles * npairs;
   // work items: (pair tile, K range); with p.splits > 1 each item covers KT / p.splits K steps and writes an fp32
-  // partial that a reduction kernel adds up; with p.tail_tiles > 0 only the last tiles are split (pair_item)
-  const int nitems = pair_items(p, ntiles);
+  // partial that a reduction kernel adds up
+  const int nitems = ntiles * p.splits;
 
   auto stage_x = [&](int s) { return smem + C::kXOff + s * XH_BYTES; };
   auto stage_a = [&](int s) { return smem + C::kAOff + s * WE_BYTES; };
@@ -847,7 +795,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
   cluster_sync();  // both CTAs' barriers and TMEM exist before any signal crosses the pair
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const int KT = p.KT;
+  const int KT = p.KT, KTs = p.KT / p.splits;
 
   if (warp == 0) {
     // ---------------- producer: this CTA's activation half and weight tile ----------------
@@ -856,13 +804,12 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
       uint32_t issued = 0, last_par = 0;
       bool ok = true;
       for (int t = cid; ok && t < nitems; t += ncl) {
-        int tt, kt0, kts, slot;
-        pair_item(p, t, ntiles, tt, kt0, kts, slot);
+        const int tt = t % ntiles, kt0 = (t / ntiles) * KTs;
         int xt, wp;
         pair_tile_coords(p, tt, npairs, xt, wp);
         const int wt = 2 * wp + static_cast<int>(rank);
         const uint8_t* wsrc = p.w9 + static_cast<int64_t>(wt) * KT * W9_BYTES;
-        for (int kt = kt0; kt < kt0 + kts; ++kt, ++kiter) {
+        for (int kt = kt0; kt < kt0 + KTs; ++kt, ++kiter) {
           const int s = kiter % S;
           const uint32_t ph = (kiter / S) & 1;
           if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) { ok = false; break; }
@@ -892,9 +839,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
         if (!mbar_wait_warp(&bars->acce[b], (use & 1) ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * 256;
-        int tt, kt0, kts, slot;
-        pair_item(p, t, ntiles, tt, kt0, kts, slot);
-        for (int kt = 0; kt < kts; ++kt, ++kiter) {   // kt: K step within the item (accumulate from its second)
+        for (int kt = 0; kt < KTs; ++kt, ++kiter) {   // kt: K step within the item (accumulate from its second)
           const int s = kiter % S;
           const uint32_t ph = (kiter / S) & 1;
           // both CTAs' expanders have decoded stage s, which they did after its loads landed
@@ -944,9 +889,7 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     int kiter = 0;
     bool ok = true;
     for (int t = cid; ok && t < nitems; t += ncl) {
-      int tt, kt0, kts, slot;
-      pair_item(p, t, ntiles, tt, kt0, kts, slot);
-      for (int kt = 0; kt < kts; ++kt, ++kiter) {
+      for (int kt = 0; kt < KTs; ++kt, ++kiter) {
         if (G > 1 && (kiter % G) != grp) continue;
         const int s = kiter % S;
         const uint32_t ph = (kiter / S) & 1;
@@ -982,9 +925,8 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
     bool ok = true;
     uint32_t rms_uses = 0;
     for (int t = cid; ok && t < nitems; t += ncl, ++it) {
-      int tt, kt0, kts, slot;
-      pair_item(p, t, ntiles, tt, kt0, kts, slot);
-      const int64_t out_off = p.tail_tiles > 0 ? 0 : static_cast<int64_t>(slot) * p.split_stride;
+      const int tt = t % ntiles;
+      const int64_t out_off = static_cast<int64_t>(t / ntiles) * p.split_stride;
       int xt, wp;
       pair_tile_coords(p, tt, npairs, xt, wp);
       const int wt = 2 * wp + static_cast<int>(rank);
@@ -1007,24 +949,6 @@ __global__ void __launch_bounds__(Cfg<V, S, G, P>::kThreads, 1)
             })) {
           ok = false;
           break;
-        }
-        continue;
-      }
-      if (p.tail_tiles > 0 && slot >= 0) {   // a tail item: its fp32 partial tile into tail_ws
-        float* tile = p.tail_ws + static_cast<int64_t>(slot) * (BN * 2 * BM);
-        const int64_t row0 = static_cast<int64_t>(xt) * BN;
-        uint32_t r[kChunk];
-#pragma unroll 1
-        for (int c = 0; c < NC; ++c) {
-          RL_TMEM_LD16(tbase + c * kChunk, r);
-          tmem_ld_wait_regs(r);
-          if (c == NC - 1) {   // the accumulator is in registers: release it
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(at_leader(&bars->acce[b]));
-          }
-          const int r0 = h * (BN / 2) + c * kChunk;
-          tail_chunk(tile, r, st, lane, q, static_cast<int>(rank), r0, p.M - (row0 + r0));
         }
         continue;
       }
@@ -1171,9 +1095,8 @@ int launch_pair(const uint16_t* x, const Params& p, cudaStream_t stream) {
   int max_clusters = 0;
   int st2 = pair_max_clusters<V, S, G, P, E>(&max_clusters);
   if (st2 != RL_OK) return st2;
-  const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2);
-  const int nitems = p.tail_tiles > 0 ? ntiles - p.tail_tiles + p.tail_tiles * p.tail_splits : ntiles * p.splits;
-  const int nclusters = nitems < max_clusters ? nitems : max_clusters;
+  const int ntiles = p.num_x_tiles * (p.num_w_tiles / 2) * p.splits;
+  const int nclusters = ntiles < max_clusters ? ntiles : max_clusters;
   cfg.gridDim = dim3(2 * nclusters);
   RL_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p));
   RL_TRY_CUDA(cudaGetLastError());
@@ -1272,69 +1195,6 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   }
 }
 
-// The tail split (pair kernel, no uniform split): when the pair tiles fill the resident clusters w times over and a
-// few more (rem <= clusters / 2), those rem tiles of the partial last wave are split into `splits` K ranges so
-// that up to all clusters share them; returns false when no such split applies.
-inline bool choose_tail(int64_t M, int64_t K, int64_t N, int* tail_tiles, int* tail_splits) {
-  if (N % 256) return false;
-  int resident = 0;
-  if (pair_max_clusters<kTmemA, 8, 2, 2>(&resident) != RL_OK || resident <= 0) return false;
-  const int64_t tiles = (M + BN - 1) / BN * (N / 256);
-  const int64_t KT = K / BK;
-  if (tiles <= resident) return false;
-  const int64_t rem = tiles % resident;
-  if (rem == 0 || 2 * rem > resident) return false;
-  int best = 1;
-  for (int64_t sp = 2; sp <= KT / 2; ++sp)
-    if (KT % sp == 0 && rem * sp <= resident) best = static_cast<int>(sp);
-  if (best < 2) return false;
-  *tail_tiles = static_cast<int>(rem);
-  *tail_splits = best;
-  return true;
-}
-
-// out[tail tiles] = sum of their tail_splits fp32 partial tiles (+ bias), to bf16 or fp32; 4 columns a thread.
-__global__ void __launch_bounds__(256) tail_reduce_kernel(const Params p, const uint16_t* __restrict__ bias,
-                                                          void* __restrict__ out, int out_f32) {
-  const int npairs = p.num_w_tiles / 2, ntiles = p.num_x_tiles * npairs, nfull = ntiles - p.tail_tiles;
-  constexpr int kTile = BN * 2 * BM;   // 256 rows x 256 columns
-  const int64_t total = static_cast<int64_t>(p.tail_tiles) * (kTile / 4);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * 256) {
-    const int j = static_cast<int>(i / (kTile / 4));
-    const int e = static_cast<int>(i % (kTile / 4)) * 4;
-    const int r = e >> 8, c = e & 255;
-    int xt, wp;
-    pair::pair_tile_coords(p, nfull + j, npairs, xt, wp);
-    const int64_t row = static_cast<int64_t>(xt) * BN + r;
-    if (row >= p.M) continue;
-    const float* src = p.tail_ws + static_cast<int64_t>(j) * p.tail_splits * kTile + e;
-    float4 a = *reinterpret_cast<const float4*>(src);
-    for (int sp = 1; sp < p.tail_splits; ++sp) {
-      const float4 b = *reinterpret_cast<const float4*>(src + static_cast<int64_t>(sp) * kTile);
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
-    }
-    const int64_t col = static_cast<int64_t>(wp) * 256 + c;
-    if (bias) {
-      a.x += bf16_bits_to_float(bias[col]);
-      a.y += bf16_bits_to_float(bias[col + 1]);
-      a.z += bf16_bits_to_float(bias[col + 2]);
-      a.w += bf16_bits_to_float(bias[col + 3]);
-    }
-    const int64_t o = row * p.N + col;
-    if (out_f32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(out) + o) = a;
-    } else {
-      const uint32_t lo = float_to_bf16_bits(a.x) | (float_to_bf16_bits(a.y) << 16);
-      const uint32_t hi = float_to_bf16_bits(a.z) | (float_to_bf16_bits(a.w) << 16);
-      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + o) = make_uint2(lo, hi);
-    }
-  }
-}
-
 }  // namespace gemm
 }  // namespace rl
 
@@ -1342,12 +1202,8 @@ extern "C" {
 
 size_t rl_linear_bfp16_workspace(int64_t M, int64_t K, int64_t N, int epilogue) {
   if (M <= 0 || K < 64 || K % 64 || N < 128 || N % 128 || epilogue == RL_EPI_SWIGLU) return 0;
-  if (M >= ((int64_t)1 << 31) || K > ((int64_t)1 << 31)) return 0;
   const int S = rl::gemm::choose_splits(M, K, N);
-  if (S > 1) return static_cast<size_t>(S) * M * N * 4;
-  int tt = 0, ts = 0;
-  if (rl::gemm::choose_tail(M, K, N, &tt, &ts)) return static_cast<size_t>(tt) * ts * 256 * 256 * 4;
-  return 0;
+  return S > 1 ? static_cast<size_t>(S) * M * N * 4 : 0;
 }
 
 int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_native, int64_t N,
@@ -1380,25 +1236,6 @@ int rl_linear_bfp16_ws(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w
   p.group_x = group_tiles(p.num_x_tiles, K);
   p.splits = choose_splits(M, K, N);
   p.split_stride = M * N;
-  int tail_tiles = 0, tail_splits = 1;
-  if (p.splits == 1 && choose_tail(M, K, N, &tail_tiles, &tail_splits)) {
-    // whole tiles through the normal epilogue (bias, output dtype), the tail tiles' partials into the workspace
-    p.bias = epilogue == RL_EPI_BIAS ? bias : nullptr;
-    p.epilogue = epilogue;
-    p.out = out;
-    p.out_f32 = out_dtype == RL_F32 ? 1 : 0;
-    p.split_stride = 0;
-    p.tail_tiles = tail_tiles;
-    p.tail_splits = tail_splits;
-    p.tail_ws = static_cast<float*>(workspace);
-    int st = launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
-    if (st != RL_OK) return st;
-    const int64_t threads = static_cast<int64_t>(tail_tiles) * 256 * 256 / 4;
-    tail_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        p, epilogue == RL_EPI_BIAS ? bias : nullptr, out, p.out_f32);
-    RL_TRY_CUDA(cudaGetLastError());
-    return RL_OK;
-  }
   int st = launch_pair<kTmemA, 8, 2, 2>(x, p, stream);
   if (st != RL_OK) return st;
   const int64_t MN = M * N;

@@ -176,59 +176,6 @@ def test_linear_split_k_small_grid(env):
     assert torch.equal(c, unsplit)
 
 
-def _tail_plan(M, K, N, clusters):
-    """The tail split's choice (rl_gemm.cu choose_tail): the rem tiles of a partial last wave split into the most K
-    ranges (a divisor of K / 64, at least 2 steps each) that rem x splits clusters can take."""
-    tiles = -(-M // 256) * (N // 256)
-    KT = K // 64
-    if N % 256 or tiles <= clusters:
-        return 0, 1
-    rem = tiles % clusters
-    if rem == 0 or 2 * rem > clusters:
-        return 0, 1
-    best = max([sp for sp in range(2, KT // 2 + 1) if KT % sp == 0 and rem * sp <= clusters], default=1)
-    return (rem, best) if best >= 2 else (0, 1)
-
-
-def test_linear_tail_split(env):
-    """The pair tiles of a partial last wave split along K over the idle clusters (rl_linear_bfp16_ws without a
-    uniform split): every other tile is computed whole, the tail tiles add their K ranges' fp32 partials; the result
-    matches the oracle on rows of every activation tile and the unsplit kernel within one bf16 step (bf16) / 1e-5
-    (fp32), most values bit for bit."""
-    torch, ops, dev = env
-    from redline_tiny_b200 import _lib as L
-    M, K, N = 700, 1024, 7168
-    clusters = L.lib().rl_gemm_pair_clusters()
-    rem, sp = _tail_plan(M, K, N, clusters)
-    if rem == 0:
-        pytest.skip(f"{clusters} resident pair clusters leave no tail to split for this shape")
-    x, W, b = _case(M, K, N, seed=13)
-    _, dq = ops.quantize_bfp16(torch.from_numpy(x).to(dev))
-    w = ops.PackedWeight.from_pack_b(torch.from_numpy(O.pack_b(W)).to(dev), K, N)
-    bt = torch.from_numpy(b).to(dev).to(torch.bfloat16)
-    need = L.lib().rl_linear_bfp16_workspace(M, K, N, L.RL_EPI_BIAS)
-    assert need == rem * sp * 256 * 256 * 4
-    ws = torch.empty(need, dtype=torch.uint8, device=dev)
-    s = torch.cuda.current_stream().cuda_stream
-    rows = np.r_[0:8, 250:262, 500:512, 690:700]
-    _, xd = O.quantize_rows(x[rows])
-    ref = O.linear(xd, O.unpack_b(O.pack_b(W), K, N), b)
-    for dt, code, tol, agree in ((torch.bfloat16, L.RL_BF16, BF16_OUT_TOL, 2.0 ** -7), (torch.float32, L.RL_F32, 2e-3, 1e-5)):
-        for _ in range(2):      # twice: the workspace holds the last call's partials
-            c = torch.full((M, N), 3.0, dtype=dt, device=dev)
-            L.call("rl_linear_bfp16_ws", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
-                   c.data_ptr(), code, ws.data_ptr(), need, s)
-        u = torch.empty((M, N), dtype=dt, device=dev)
-        L.call("rl_linear_bfp16", dq.data_ptr(), M, K, w.native.data_ptr(), N, bt.data_ptr(), L.RL_EPI_BIAS,
-               u.data_ptr(), code, s)
-        ops.device_status()
-        got = c.float().cpu().numpy()[rows]
-        assert O.max_rel(got, ref) <= tol, _diag(got, ref)
-        assert (c.float() - u.float()).abs().max().item() <= agree * u.float().abs().max().item()
-        same = (c == u).float().mean().item()
-        assert same >= 1.0 - rem / (-(-M // 256) * (N // 256)), f"only {same:.3f} of the values equal the unsplit run"
-
-
 def test_linear_grouped_tile_order(env):
     """Pair tiles walk groups of activation tiles sized to ~40 MB of X: at K = 12288 a group is 6 tiles at most, so
     19 activation tiles (ragged M) form groups of 5, 5, 5 and 4; every tile is computed once and correctly (oracle
