@@ -201,6 +201,24 @@ def cpu_baseline_sample():
     return FLOP / dt / 1e12, dt, ref.cores
 
 
+def cpu_dit_block_sample():
+    """The DiT step's host path (the CPU oracle of the block math, oracle/dit_oracle.py, numpy on every host core) on
+    config 4's shapes with one block, once: seconds (the embedding, one block and the projection; a 32-block step
+    is estimated as 32 x this), and the thread count."""
+    import numpy as np
+    import torch
+    from oracle import dit_oracle as DO
+    from redline_tiny_b200 import dit, host_glue as HG
+    cfg = dit.DiTConfig(blocks=1)
+    prep = DO.prepare(dit.random_weights(cfg, seed=0, device="cpu"))
+    rng = np.random.default_rng(0)
+    lat = rng.standard_normal((cfg.image, cfg.latent_ch)).astype(np.float32)
+    txt = rng.standard_normal((cfg.text, cfg.hidden)).astype(np.float32)
+    t = time.perf_counter()
+    DO.forward(cfg, prep, lat, txt, HG.SIGMAS[3], HG)
+    return time.perf_counter() - t, _blas_threads()
+
+
 def run_reference(args, ws, rank):
     if rank != 0:          # under torchrun rank 0 alone times the host path; the others exit without work
         return
@@ -856,6 +874,16 @@ def run_ours(args, ws, rank, local):
         res["cpu_baseline"] = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                "sample": f"config 1 in full ({M} rows) once: to_bfp16(a_layout) + from_bfp16 + "
                                          f"float32 matmul with bias, numpy/OpenBLAS on {cores} threads, {dt:.2f} s"}
+        if not args.no_extras:
+            bt, bcores = cpu_dit_block_sample()
+            c4 = {"one_block_s": bt, "step_estimate_ms": 32e3 * bt, "cores": bcores,
+                  "sample": "config 4's shapes with one block (embedding + block + projection), the CPU oracle of "
+                            "the block math once; the 32-block step estimated as 32 x that"}
+            gpu_ms = extras.get("C4_dit_step", {}).get("ms")
+            if gpu_ms:
+                c4["gpu_step_ms"] = gpu_ms
+                c4["gpu_speedup"] = 32e3 * bt / gpu_ms
+            res["cpu_baseline"]["c4_dit_step"] = c4
     res["parity_ok"] = not failures
     if failures:
         res["parity_failures"] = failures
