@@ -15,7 +15,11 @@ import types
 import numpy as np
 import pytest
 
-REF = "/root/reference/redline"
+# the reference checkout's redline/ directory: REDLINE_REFERENCE names the checkout (as make_golden.py's argument
+# does); without it the test looks beside this repository
+REF = os.path.join(os.environ.get("REDLINE_REFERENCE",
+                                  os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "reference")),
+                   "redline")
 
 
 def _forward_module():
