@@ -590,11 +590,11 @@ def measure_configs(dev, stream, ws, rank):
     out["next_rows"] = measure_next_rows(dev, stream, 100 + rank)
     if ws > 1:   # config 4 again, tensor-parallel over all ranks at batch 1
         import torch.distributed as dist
-        # the default reduction (at 2 GPUs the projection GEMM stores its bf16 partial into the other rank's memory
-        # and the LayerNorm kernel adds both; above 2 the same GEMM stores each row block into its owner's memory,
-        # the owner's LayerNorm adds them and stores its rows into every rank's next A operand), and beside it the
-        # other forms: at 2 GPUs the peer reduce-scatter form and NCCL's bf16 all-reduce, above 2 NCCL's bf16
-        # all-reduce and its reduce-scatter + all-gather; and NCCL's all-reduce of fp32 partials. Parity:
+        # the default reduction (the projection GEMM stores each row block of its partial into the memory of the
+        # rank that owns those rows, the owner's LayerNorm adds them and stores its rows into every rank's next A
+        # operand), and beside it the other forms: at 2 GPUs the peer all-reduce (the GEMM stores its whole partial
+        # into the other rank, both LayerNorms add both) and NCCL's bf16 all-reduce, above 2 NCCL's bf16 all-reduce
+        # and its reduce-scatter + all-gather; and NCCL's all-reduce of fp32 partials. Parity:
         # the TP velocity against the unsharded model's on the same weights and inputs. Partials rounded to bf16
         # before they are added move every branch value by up to half a bf16 step, and the unsharded model itself
         # moves as far when its text input moves by half a bf16 step (velocity_cos_under_half_ulp_input_change), so
@@ -607,8 +607,8 @@ def measure_configs(dev, stream, ws, rank):
                  "rs": "NCCL reduce-scatter + LayerNorm on M/N rows + NCCL all-gather",
                  "bf16": "NCCL all-reduce, bf16 (LayerNorm replicated)",
                  "fp32": "NCCL all-reduce, fp32 partials (LayerNorm replicated)"}
-        # "auto" is "peer" at 2 GPUs and "peer_rs" above; the other forms are timed and checked beside it
-        for mode in (("auto", "peer_rs", "bf16", "fp32") if ws == 2 else ("auto", "bf16", "rs", "fp32")):
+        # "auto" is "peer_rs"; the other forms are timed and checked beside it
+        for mode in (("auto", "peer", "bf16", "fp32") if ws == 2 else ("auto", "bf16", "rs", "fp32")):
             w = dit.random_weights(cfg, seed=1000)       # the same weights on every rank, then this rank's shard
             tp_model = dit.DiT(cfg, dit.shard_weights(w, cfg, rank, ws), device=dev, tp=(rank, ws, dist.group.WORLD),
                                reduce_dtype=mode)
@@ -623,8 +623,8 @@ def measure_configs(dev, stream, ws, rank):
             dt = HG.SIGMAS[4] - HG.SIGMAS[3]     # the Euler step this velocity feeds (forward.py:58-61)
             lcos = _cos(lat_tp + dt * v, lat_tp + dt * v_ref)
             worst = _max_over_ranks([-cos, err, -lcos], dev, ws)
-            key = f"C4_dit_step_tp{ws}" + {"auto": "", "peer_rs": "_peer_rs", "bf16": "_nccl_bf16", "rs": "_nccl_rs",
-                                           "fp32": "_nccl_fp32"}[mode]
+            key = f"C4_dit_step_tp{ws}" + {"auto": "", "peer": "_peer_allreduce", "peer_rs": "_peer_rs",
+                                           "bf16": "_nccl_bf16", "rs": "_nccl_rs", "fp32": "_nccl_fp32"}[mode]
             bar = COS_BAR if mode == "fp32" else min(COS_BAR, 1.0 - 2.0 * (1.0 - floor))
             e = {"ms": ms, "TFLOP/s_all_gpus": cfg.flop_per_step() / (ms * 1e-3) / 1e12,
                  "reductions_per_step": 2 * cfg.blocks,
@@ -638,7 +638,7 @@ def measure_configs(dev, stream, ws, rank):
                 failures.append(f"{key}: velocity cosine {-worst[0]:.6f} < {bar:.6f}")
             if -worst[2] < COS_BAR:
                 failures.append(f"{key}: latent cosine {-worst[2]:.6f} < {COS_BAR}")
-            if mode in ("auto", "peer_rs"):
+            if mode in ("auto", "peer"):
                 totals, block = launch_breakdown(tp_model, lambda: tp_model.denoise_step(lat_tp, txt_tp, 3), stream)
                 e["launches_per_step"] = totals
                 e["block10_us"] = block
@@ -647,8 +647,8 @@ def measure_configs(dev, stream, ws, rank):
             del tp_model
             torch.cuda.empty_cache()
         if ws == 2:
-            same = bool(torch.equal(v_modes["auto"], v_modes["bf16"]))
-            out[f"C4_dit_step_tp{ws}"]["peer_sum_equals_nccl_bf16_allreduce"] = same
+            same = bool(torch.equal(v_modes["peer"], v_modes["bf16"]))
+            out[f"C4_dit_step_tp{ws}_peer_allreduce"]["peer_sum_equals_nccl_bf16_allreduce"] = same
             if not same:
                 failures.append("TP-2: the peer reduction's velocity differs from NCCL's bf16 all-reduce")
     L.device_status()      # raises if any kernel recorded a device-side error

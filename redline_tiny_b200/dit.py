@@ -121,9 +121,9 @@ class DiT:
     block of its partial straight into the owning rank's memory as it computes it, the LayerNorm kernel of the owner
     adds the partials of its rows and stores its rows of the output into every rank's A operand: tp.PeerRS),
     "bf16" (one NCCL all-reduce of the bf16 partials, LayerNorm replicated), "fp32" (NCCL, fp32 partials) or "auto"
-    (default: "peer" at 2 GPUs - 27.8 against 28.1 ms per config-4 step for "peer_rs" and 29.5 for "bf16" -, and
-    "peer_rs" above when the rows split into multiples of 16, else "bf16": at 4 GPUs 17.8 ms against 22.2 for "bf16"
-    and 22.7 for "rs").
+    (default: "peer_rs" when the rows split into multiples of 16 - per config-4 step 27.6 ms at 2 GPUs against 29.2
+    for "peer" and 29.8 for "bf16", 17.8 ms at 4 GPUs against 22.2 for "bf16" and 22.7 for "rs" -, else "peer" at
+    2 GPUs and "bf16" above).
     fuse_qkv: QK-RMSNorm + RoPE run in the QKV GEMM's epilogue (rl_qkv_linear) instead of rl_qkv_post after the
     GEMM."""
 
@@ -132,10 +132,10 @@ class DiT:
             raise ValueError(f"reduce_dtype must be 'auto', 'peer', 'peer_rs', 'rs', 'bf16' or 'fp32', "
                              f"not {reduce_dtype!r}")
         if reduce_dtype == "auto":
-            if tp and tp[1] == 2:
-                reduce_dtype = "peer"
+            if tp and cfg.M % tp[1] == 0 and (cfg.M // tp[1]) % 16 == 0:
+                reduce_dtype = "peer_rs"
             else:
-                reduce_dtype = "peer_rs" if tp and cfg.M % tp[1] == 0 and (cfg.M // tp[1]) % 16 == 0 else "bf16"
+                reduce_dtype = "peer" if tp and tp[1] == 2 else "bf16"
         if tp and reduce_dtype == "rs" and cfg.M % tp[1]:
             raise ValueError(f"reduce_dtype 'rs' needs M ({cfg.M}) divisible by the group size {tp[1]}")
         if tp and reduce_dtype == "peer_rs" and (cfg.M % tp[1] or (cfg.M // tp[1]) % 16):
