@@ -1,6 +1,8 @@
-"""Peer-memory reduction for the 2-GPU tensor-parallel DiT: the all-reduce of the out- and down-projection partials
-fused into the projection GEMM (which stores its partial into the other rank's memory as it computes it) and the
-residual + LayerNorm kernel (which adds the two partials: rl_ln_mod_tp).
+"""Peer-memory reductions for the tensor-parallel DiT. PeerRS (W ranks, the default): a reduce-scatter done by the
+projection GEMM's own stores, a row-sharded LayerNorm and an all-gather done by that LayerNorm's stores (its
+docstring below). PeerReduce (2 ranks): the all-reduce of the out- and down-projection partials fused into the
+projection GEMM (which stores its partial into the other rank's memory as it computes it) and the residual +
+LayerNorm kernel (which adds the two partials: rl_ln_mod_tp), described here.
 
 The tensor-parallel DiT (the reference itself runs on one device) sums the row-split projections' partial outputs
 across ranks before each residual + LayerNorm (one reduction per sublayer, two per block). Here each rank's projection GEMM writes its bf16
