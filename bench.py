@@ -902,7 +902,8 @@ def run_ours(args, ws, rank, local):
 # ------------------------------------------------------------------------------------------------------------------
 
 CASES = ("linear_c1", "quantize_c1", "linear_m17408", "swiglu_mlp_c2", "swiglu_up_c2", "attention_c3", "qkv_post_c3",
-         "qkv_gemm_c4", "qkv_linear_c4", "ln_mod_c4", "dit_block_c4", "vae_conv_128x1152", "vae_conv_512x288")
+         "qkv_gemm_c4", "qkv_linear_c4", "ln_mod_c4", "dit_block_c4", "vae_conv_128x1152", "vae_conv_512x288",
+         "scatter_gemm_tp2", "ln_rows_tp2")
 
 
 def run_case(case, iters):
@@ -943,6 +944,35 @@ def run_case(case, iters):
                 ops.swiglu_up(x, w, out=h)
             else:
                 ops.swiglu_mlp(x, w, wd, out=o, workspace=wsp)
+    elif c in ("scatter_gemm_tp2", "ln_rows_tp2"):
+        # the peer reduce-scatter's two kernels at TP-2 shapes, with both "ranks'" buffers on this GPU: the out
+        # projection of 12 heads scattering its partial rows (K 1536), and the row-sharded LayerNorm over 2176 rows
+        # adding two partials and storing its rows into two A operands (the wait is satisfied before the launch)
+        Mc, D = 4352, 3072
+        R = Mc // 2
+        if c == "scatter_gemm_tp2":
+            Kc = 1536
+            x = ops.quantize_bfp16(torch.randn((Mc, Kc), generator=g, device=dev), want_bytes=False)[1]
+            w = ops.PackedWeight.from_float(torch.randn((Kc, D), generator=g, device=dev) * 0.02)
+            bufs = [torch.empty(R * D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            dsts = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device=dev)
+
+            def fn():
+                L.call("rl_linear_bfp16_scatter", x.data_ptr(), Mc, Kc, w.native.data_ptr(), D, dsts.data_ptr(), 2, R,
+                       s)
+        else:
+            xin = torch.randn((R, D), generator=g, device=dev).to(torch.bfloat16)
+            parts = [torch.randn((R * D,), generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+            parts_t = torch.tensor([t.data_ptr() for t in parts], dtype=torch.int64, device=dev)
+            pad = torch.tensor([1 << 40, 0], dtype=torch.int64, device=dev)   # rank 1 sees rank 0's epoch
+            params = (1 + 0.1 * torch.randn((2, 2, D), generator=g, device=dev)).to(torch.bfloat16)
+            xo = torch.empty((R, D), dtype=torch.bfloat16, device=dev)
+            outs = [torch.empty((Mc, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            y_dsts = torch.tensor([t[R:].data_ptr() for t in outs], dtype=torch.int64, device=dev)
+
+            def fn():
+                L.call("rl_ln_mod_tp_rs", xin.data_ptr(), parts_t.data_ptr(), 2, pad.data_ptr(), 1, 1,
+                       params.data_ptr(), R, D, 0, xo.data_ptr(), y_dsts.data_ptr(), s)
     elif c in ("vae_conv_128x1152", "vae_conv_512x288"):
         H, C = (128, 1152) if c == "vae_conv_128x1152" else (512, 288)
         x = ops.quantize_bfp16(torch.randn((H * H, C), generator=g, device=dev), want_bytes=False)[1].view(H, H, C)
