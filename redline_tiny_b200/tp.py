@@ -110,6 +110,30 @@ class _DeviceArray:
                                          "version": 3, "strides": None}
 
 
+def peer_rs_layout(M, D, world, rank, bases):
+    """The addresses PeerRS hands to the kernels, from every rank's allocation base (`bases`, one int per rank):
+    {"bytes": the allocation size, "R": rows per rank, "a_off": offset of the gathered A operand,
+    "pad_off": offset of the signal pads, "dsts": [slot][owner] -> where this rank's partial rows for `owner` go
+    (in the owner's allocation), "parts": [slot][src] -> this rank's received partial of rank `src`,
+    "y_dsts": [owner] -> row R * rank of the owner's A operand, "pads": [owner] -> the owner's pad base}."""
+    if M % world or (M // world) % 16:
+        raise ValueError(f"peer_rs needs M / world to be a multiple of 16 (M={M}, world={world})")
+    R = M // world
+    recv_bytes = (R * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+    a_off = 2 * world * recv_bytes
+    pad_off = a_off + (M * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
+    total = pad_off + (3 * world * 8 + _ALIGN - 1) // _ALIGN * _ALIGN
+
+    def recv(b, s, src):
+        return b + (s * world + src) * recv_bytes
+
+    return {"bytes": total, "R": R, "recv_bytes": recv_bytes, "a_off": a_off, "pad_off": pad_off,
+            "dsts": [[recv(bases[o], s, rank) for o in range(world)] for s in range(2)],
+            "parts": [[recv(bases[rank], s, w) for w in range(world)] for s in range(2)],
+            "y_dsts": [b + a_off + rank * R * D * 2 for b in bases],
+            "pads": [b + pad_off for b in bases]}
+
+
 class PeerRS:
     """Reduce-scatter + row-sharded LayerNorm + all-gather over peer memory for W ranks (reduce_dtype "peer_rs").
 
@@ -129,15 +153,12 @@ class PeerRS:
 
     def __init__(self, group, rank, world, M, D, device):
         import torch.distributed as dist
-        if M % world or (M // world) % 16:
-            raise ValueError(f"peer_rs needs M / world to be a multiple of 16 (M={M}, world={world})")
+        lay = peer_rs_layout(M, D, world, rank, [0] * world)       # sizes first: nothing allocated if they fail
         self.rank, self.world, self.M, self.D = rank, world, M, D
-        self.R = M // world
+        self.R = lay["R"]
         self.r0 = rank * self.R
-        self.recv_bytes = (self.R * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
-        self.a_off = 2 * world * self.recv_bytes
-        self.pad_off = self.a_off + (M * D * 2 + _ALIGN - 1) // _ALIGN * _ALIGN
-        total = self.pad_off + (3 * world * 8 + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.a_off, self.pad_off = lay["a_off"], lay["pad_off"]
+        total = lay["bytes"]
         ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
         L.call("rl_ipc_alloc", total, ctypes.byref(ptr), handle)
         self.base = ptr.value
@@ -158,15 +179,12 @@ class PeerRS:
             self.close()
             raise
         i64 = dict(dtype=torch.int64, device=device)
-
-        def recv(b, s, src):
-            return b + (s * world + src) * self.recv_bytes
-
+        lay = peer_rs_layout(M, D, world, rank, bases)
         # slot s: where this rank's partial rows for owner o go, and this rank's W received partials
-        self.dsts = [torch.tensor([recv(bases[o], s, rank) for o in range(world)], **i64) for s in range(2)]
-        self.parts = [torch.tensor([recv(self.base, s, w) for w in range(world)], **i64) for s in range(2)]
-        self.y_dsts = torch.tensor([b + self.a_off + self.r0 * D * 2 for b in bases], **i64)
-        self.pads = torch.tensor([b + self.pad_off for b in bases], **i64)
+        self.dsts = [torch.tensor(lay["dsts"][s], **i64) for s in range(2)]
+        self.parts = [torch.tensor(lay["parts"][s], **i64) for s in range(2)]
+        self.y_dsts = torch.tensor(lay["y_dsts"], **i64)
+        self.pads = torch.tensor(lay["pads"], **i64)
         self.a = torch.as_tensor(_DeviceArray(self.base + self.a_off, M, D), device=device).view(torch.bfloat16)
         self.epoch = 0
         self.group = group

@@ -77,3 +77,35 @@ def test_reduction_choice_is_checked():
         dit.DiT(dit.DiTConfig(blocks=1), {}, device="cpu", reduce_dtype="fp16")
     with pytest.raises(ValueError, match="2 ranks"):
         tp.PeerReduce(None, 0, 4, 64, 256, "cpu")
+
+
+def test_peer_rs_layout():
+    """The peer reduce-scatter's buffers for 2 to 8 ranks at config 4 (and a toy size): inside each rank's
+    allocation, 256-byte aligned, non-overlapping; every rank's scatter destination for owner o is that owner's
+    receive buffer of the sender; the all-gather destinations are the sender's rows of every operand."""
+    from redline_tiny_b200 import tp
+    for M, D in ((4352, 3072), (256, 256)):
+        for W in range(2, 9):
+            if M % W or (M // W) % 16:
+                continue
+            bases = [(1 + r) << 40 for r in range(W)]            # far apart: any spill into a neighbour shows
+            lays = [tp.peer_rs_layout(M, D, W, r, bases) for r in range(W)]
+            L0 = lays[0]
+            R = M // W
+            assert L0["R"] == R and L0["recv_bytes"] >= R * D * 2
+            regions = [(s * W + src) * L0["recv_bytes"] for s in range(2) for src in range(W)]
+            ends = [o + R * D * 2 for o in regions]
+            assert all(e <= n for e, n in zip(ends, regions[1:] + [L0["a_off"]]))
+            assert L0["a_off"] + M * D * 2 <= L0["pad_off"] and L0["pad_off"] + 3 * W * 8 <= L0["bytes"]
+            for r, lay in enumerate(lays):
+                for s in range(2):
+                    for o in range(W):
+                        assert lay["dsts"][s][o] == lays[o]["parts"][s][r]      # sender r -> owner o, slot s
+                        assert lay["dsts"][s][o] % 256 == 0
+                        assert bases[o] <= lay["dsts"][s][o] < bases[o] + L0["a_off"]
+                for o in range(W):
+                    assert lay["y_dsts"][o] == bases[o] + L0["a_off"] + r * R * D * 2
+                    assert lay["pads"][o] == bases[o] + L0["pad_off"]
+    import pytest
+    with pytest.raises(ValueError):
+        tp.peer_rs_layout(4352, 3072, 5, 0, [0] * 5)
