@@ -354,7 +354,9 @@ int rl_tp_signal(void* const* pads, int W, int rank, int slot, unsigned long lon
  * of W pointers: rank o's receive buffer for this rank's partial; peers over NVLink); every value crosses to its
  * owner once. rl_ln_mod_tp_rs: rl_ln_mod_tp over this rank's R rows (x, x_out: R x D; parts: the W received partials,
  * R-row chunk layout, summed in rank order; row_split relative to the block) that stores y into every rank's copy of
- * the next GEMM's A operand (y_dsts: device array of W pointers to row r0 = rank x R of each copy). rl_tp_wait: a
+ * the next GEMM's A operand (y_dsts: device array of W pointers to row r0 = rank x R of each copy). Every pointer
+ * inside dsts, parts and y_dsts must be 16-byte aligned (the kernels cannot check device-resident pointers; a
+ * cudaMalloc / rl_ipc_alloc base plus offsets that are multiples of 16 bytes, as tp.PeerRS builds them). rl_tp_wait: a
  * bounded wait on the stream until every other rank's entry of pad (this rank's, W uint64) reaches epoch; it runs
  * between rl_tp_signal of the all-gather and the GEMM that reads the gathered rows. On a timeout the kernel records
  * the error for rl_device_status and returns. */
